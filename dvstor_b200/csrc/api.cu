@@ -1,0 +1,530 @@
+// C ABI of the query path: index lifetime, device layout upload, search
+// orchestration and the kernel-level entry points.  Replaces the reference's
+// GPU launcher (src/gpu/gpu_kernel_launcher.cu) and per-coroutine buffer
+// manager (src/gpu/gpu_buffer_manager.cu) for queries: the library owns the
+// device copy of the index and every scratch buffer, and reports failures as
+// status codes instead of abort().
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+#include "internal.h"
+#include "search.cuh"
+
+using dvs::fail;
+
+namespace dvs {
+namespace {
+
+#define DVS_CUDA(call)                                                                             \
+  do {                                                                                             \
+    const cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess) {                                                                       \
+      return fail(e_ == cudaErrorMemoryAllocation ? DVS_ERR_OOM : DVS_ERR_CUDA,                    \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                             \
+    }                                                                                              \
+  } while (0)
+
+template <class T>
+void dev_free(T*& p) {
+  if (p) cudaFree(p);
+  p = nullptr;
+}
+
+// Visited-set sizing: default shared-memory slots per beam entry and the spill table.
+constexpr uint32_t kDefaultSlotsPerBeamEntry = 48;
+constexpr uint32_t kOverflowSlots = 1u << 16;
+
+struct Device {
+  int ordinal = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  uint32_t sm_count = 0;
+  // index
+  uint32_t* adj = nullptr;
+  uint32_t* rec = nullptr;
+  float* vecs = nullptr;
+  uint32_t* ids = nullptr;
+  float* P = nullptr;
+  float* c_rot = nullptr;
+  DevLayout lay;
+  // scratch
+  size_t q_cap = 0;        // queries the scratch holds
+  size_t out_cap = 0;      // result slots the host-path buffers hold
+  float* queries = nullptr;
+  float* qrot = nullptr;
+  float* qfac = nullptr;
+  uint32_t* out_ids = nullptr;
+  float* out_dist = nullptr;
+  uint32_t* counters = nullptr;
+  uint32_t* work = nullptr;
+  uint32_t* ovf = nullptr;
+  size_t ovf_slots = 0;
+
+  void release() {
+    if (ordinal < 0) return;
+    cudaSetDevice(ordinal);
+    dev_free(adj);
+    dev_free(rec);
+    dev_free(vecs);
+    dev_free(ids);
+    dev_free(P);
+    dev_free(c_rot);
+    dev_free(queries);
+    dev_free(qrot);
+    dev_free(qfac);
+    dev_free(out_ids);
+    dev_free(out_dist);
+    dev_free(counters);
+    dev_free(work);
+    dev_free(ovf);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+    ev0 = ev1 = nullptr;
+    stream = nullptr;
+  }
+};
+
+struct LaunchShape {
+  uint32_t cap = 0, cap_pad = 0, hcap = 0, wpb = 0, blocks_per_sm = 0;
+};
+
+dvs_status upload(Device& d, const HostIndex& h) {
+  const dvs_index_info& in = h.info;
+  const uint64_t n = in.num_vectors;
+  const uint32_t dim = in.dim, R = in.R, bits = in.rabitq_bits;
+  const uint32_t packed = (bits * dim + 7) / 8;
+  const uint32_t code_words = (packed + 3) / 4;
+  const uint32_t rec_words = (code_words + 2 + 3) / 4 * 4;
+  const uint32_t vec_stride = (dim + 3) / 4 * 4;
+  DVS_CUDA(cudaSetDevice(d.ordinal));
+  int sms = 0;
+  DVS_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d.ordinal));
+  d.sm_count = uint32_t(sms);
+  DVS_CUDA(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+  DVS_CUDA(cudaEventCreate(&d.ev0));
+  DVS_CUDA(cudaEventCreate(&d.ev1));
+  // records: reference layout -> [codes | pad to word | add | rescale | pad to 16 B]
+  std::vector<uint32_t> rec(size_t(n) * rec_words, 0u);
+  for (uint64_t g = 0; g < n; ++g) {
+    const uint8_t* src = h.records.data() + g * in.rabitq_size;
+    uint8_t* dst = reinterpret_cast<uint8_t*>(rec.data() + g * rec_words);
+    std::memcpy(dst, src, packed);
+    std::memcpy(dst + size_t(code_words) * 4, src + packed, 8);
+  }
+  std::vector<float> vecs;
+  const float* vsrc = h.vecs.data();
+  if (vec_stride != dim) {
+    vecs.assign(size_t(n) * vec_stride, 0.f);
+    for (uint64_t g = 0; g < n; ++g) std::memcpy(&vecs[g * vec_stride], &h.vecs[g * dim], size_t(dim) * 4);
+    vsrc = vecs.data();
+  }
+  DVS_CUDA(cudaMalloc(&d.adj, size_t(n) * R * 4));
+  DVS_CUDA(cudaMalloc(&d.rec, rec.size() * 4));
+  DVS_CUDA(cudaMalloc(&d.vecs, size_t(n) * vec_stride * 4));
+  DVS_CUDA(cudaMalloc(&d.ids, size_t(n) * 4));
+  DVS_CUDA(cudaMalloc(&d.P, size_t(dim) * dim * 4));
+  DVS_CUDA(cudaMalloc(&d.c_rot, size_t(dim) * 4));
+  DVS_CUDA(cudaMemcpy(d.adj, h.adj.data(), size_t(n) * R * 4, cudaMemcpyHostToDevice));
+  DVS_CUDA(cudaMemcpy(d.rec, rec.data(), rec.size() * 4, cudaMemcpyHostToDevice));
+  DVS_CUDA(cudaMemcpy(d.vecs, vsrc, size_t(n) * vec_stride * 4, cudaMemcpyHostToDevice));
+  DVS_CUDA(cudaMemcpy(d.ids, h.ids.data(), size_t(n) * 4, cudaMemcpyHostToDevice));
+  DVS_CUDA(cudaMemcpy(d.P, h.rotation.data(), size_t(dim) * dim * 4, cudaMemcpyHostToDevice));
+  DVS_CUDA(cudaMemcpy(d.c_rot, h.rotated_centroid.data(), size_t(dim) * 4, cudaMemcpyHostToDevice));
+  DVS_CUDA(cudaMalloc(&d.work, 16));
+  DevLayout& L = d.lay;
+  L.adj = d.adj;
+  L.rec = d.rec;
+  L.vecs = d.vecs;
+  L.ids = d.ids;
+  L.P = d.P;
+  L.c_rot = d.c_rot;
+  L.n = n;
+  L.dim = dim;
+  L.R = R;
+  L.bits = bits;
+  L.medoid = in.medoid;
+  L.metric = in.metric == DVS_METRIC_IP ? 1u : 0u;
+  L.rec_words = rec_words;
+  L.code_words = code_words;
+  L.vec_stride = vec_stride;
+  return DVS_OK;
+}
+
+dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path) {
+  const size_t vs = d.lay.vec_stride;
+  if (nq > d.q_cap) {
+    const size_t cap = std::max(nq, d.q_cap * 2);
+    dev_free(d.queries);
+    dev_free(d.qrot);
+    dev_free(d.qfac);
+    dev_free(d.counters);
+    DVS_CUDA(cudaMalloc(&d.queries, cap * d.lay.dim * 4));
+    DVS_CUDA(cudaMalloc(&d.qrot, cap * vs * 4));
+    DVS_CUDA(cudaMalloc(&d.qfac, cap * 16));
+    DVS_CUDA(cudaMalloc(&d.counters, cap * 16));
+    d.q_cap = cap;
+  }
+  if (host_path && nq * k > d.out_cap) {
+    const size_t cap = std::max(nq * k, d.out_cap * 2);
+    dev_free(d.out_ids);
+    dev_free(d.out_dist);
+    DVS_CUDA(cudaMalloc(&d.out_ids, cap * 4));
+    DVS_CUDA(cudaMalloc(&d.out_dist, cap * 4));
+    d.out_cap = cap;
+  }
+  return DVS_OK;
+}
+
+dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, LaunchShape& s) {
+  s.cap = cap;
+  s.cap_pad = (cap + 31) / 32 * 32;
+  s.hcap = std::max(64u, (cap * slots_per_entry + 31) / 32 * 32);
+  const uint32_t words = search_warp_words(s.cap_pad, d.lay.vec_stride, s.hcap);
+  int best_warps = 0;
+  for (uint32_t wpb : {1u, 2u, 4u, 8u}) {
+    const size_t smem = size_t(wpb) * words * 4;
+    if (smem > 227 * 1024) break;
+    int bps = 0;
+    const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, wpb, smem, &bps);
+    if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
+    if (int(wpb) * bps > best_warps) {
+      best_warps = int(wpb) * bps;
+      s.wpb = wpb;
+      s.blocks_per_sm = uint32_t(bps);
+    }
+  }
+  if (best_warps == 0)
+    return fail(DVS_ERR_CAPACITY, "beam capacity " + std::to_string(cap) + " needs more shared memory than a block has");
+  // set the attribute for the chosen configuration last
+  int bps = 0;
+  const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, s.wpb, size_t(s.wpb) * words * 4, &bps);
+  if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
+  return DVS_OK;
+}
+
+}  // namespace
+}  // namespace dvs
+
+struct dvs_index {
+  dvs::HostIndex host;              // kept for downloads and metadata
+  std::vector<dvs::Device> devs;
+  uint32_t hop_limit = 0;
+  uint32_t slots_per_entry = dvs::kDefaultSlotsPerBeamEntry;
+  std::mutex mu;
+};
+
+namespace dvs {
+namespace {
+
+// Prepare + search for nq device-resident queries on one device.
+dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L, dvs_mode mode,
+                     uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st, bool timed) {
+  const DevLayout& lay = d.lay;
+  const bool rabitq = mode == DVS_MODE_RABITQ_GPU;
+  if (rabitq && lay.bits != 1 && lay.bits != 2 && lay.bits != 4)
+    return fail(DVS_ERR_BITS, "rabitq_gpu search supports 1-, 2- and 4-bit codes on the device; index has " +
+                                  std::to_string(lay.bits));
+  if (lay.R > 64) return fail(DVS_ERR_UNSUPPORTED, "max out-degree above 64 is not supported by the search kernel");
+  const uint32_t cap = rabitq ? L + kBeamSlack : L;
+  LaunchShape s;
+  dvs_status rc = launch_shape(d, cap, ix->slots_per_entry, s);
+  if (rc != DVS_OK) return rc;
+  rc = ensure_scratch(d, nq, k, false);
+  if (rc != DVS_OK) return rc;
+  const uint32_t blocks_full = s.blocks_per_sm * d.sm_count;
+  const uint32_t blocks_needed = (nq + s.wpb - 1) / s.wpb;
+  const uint32_t blocks = std::max(1u, std::min(blocks_full, blocks_needed));
+  const size_t slots = size_t(blocks) * s.wpb;
+  if (slots > d.ovf_slots) {
+    dev_free(d.ovf);
+    DVS_CUDA(cudaMalloc(&d.ovf, slots * kOverflowSlots * 4));
+    d.ovf_slots = slots;
+  }
+  DVS_CUDA(cudaMemsetAsync(d.work, 0, 16, st));
+  if (timed) DVS_CUDA(cudaEventRecord(d.ev0, st));
+  if (rabitq) {
+    DVS_CUDA(launch_prepare(d_q, lay.dim, lay.P, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits, nq,
+                            st));
+  }
+  SearchArgs a;
+  a.ix = lay;
+  a.queries = d_q;
+  a.qrot = d.qrot;
+  a.qfac = d.qfac;
+  a.nq = nq;
+  a.k = k;
+  a.L = L;
+  a.cap = cap;
+  a.mode = rabitq ? 0u : 1u;
+  a.hop_limit = ix->hop_limit;
+  a.out_ids = d_ids;
+  a.out_dist = d_dist;
+  a.counters = d_counters ? d_counters : d.counters;
+  a.work = d.work;
+  a.ovf = d.ovf;
+  a.ovf_cap = kOverflowSlots;
+  a.ovf_limit = kOverflowSlots / 10 * 8;
+  a.hcap = s.hcap;
+  a.hlimit = s.hcap / 10 * 8;
+  a.cap_pad = s.cap_pad;
+  a.dim_pad = lay.vec_stride;
+  DVS_CUDA(launch_search(a, s.wpb, blocks, st));
+  if (timed) DVS_CUDA(cudaEventRecord(d.ev1, st));
+  return DVS_OK;
+}
+
+dvs_status check_query_args(const dvs_index* ix, uint32_t nq, uint32_t dim, uint32_t k, uint32_t L, dvs_mode mode) {
+  if (!ix) return fail(DVS_ERR_ARG, "null index");
+  if (mode != DVS_MODE_RABITQ_GPU && mode != DVS_MODE_EXACT_GPU)
+    return fail(DVS_ERR_ARG, "search-mode must be exact_gpu or rabitq_gpu");
+  if (dim != ix->host.info.dim)
+    return fail(DVS_ERR_DIM, "search dimension mismatch: index " + std::to_string(ix->host.info.dim) + ", query " +
+                                 std::to_string(dim));
+  if (k == 0) return fail(DVS_ERR_ARG, "k must be > 0");
+  if (L < k) return fail(DVS_ERR_ARG, "beam_width must be >= k");
+  if (L > 4096) return fail(DVS_ERR_ARG, "beam_width above 4096 is not supported");
+  (void)nq;
+  return DVS_OK;
+}
+
+}  // namespace
+}  // namespace dvs
+
+extern "C" {
+
+int dvs_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+dvs_status dvs_open(const dvs_open_params* p, dvs_index** out) {
+  if (!p || !out || !p->index_prefix) return fail(DVS_ERR_ARG, "null argument");
+  *out = nullptr;
+  if (p->placement != DVS_PLACE_REPLICATE)
+    return fail(DVS_ERR_UNSUPPORTED, "only replicated placement is available in this build");
+  const int ndev_vis = dvs_device_count();
+  if (ndev_vis == 0) return fail(DVS_ERR_NO_DEVICE, "no CUDA device is visible");
+  std::vector<int> devs;
+  const uint32_t nd = p->num_devices ? p->num_devices : 1;
+  for (uint32_t i = 0; i < nd; ++i) {
+    const int o = p->devices ? p->devices[i] : int(i);
+    if (o < 0 || o >= ndev_vis) return fail(DVS_ERR_ARG, "device ordinal " + std::to_string(o) + " is not visible");
+    devs.push_back(o);
+  }
+  auto* ix = new (std::nothrow) dvs_index;
+  if (!ix) return fail(DVS_ERR_OOM, "host allocation failed");
+  dvs_status s = dvs::load_host_index(p->index_prefix, ix->host);
+  const dvs_index_info& in = ix->host.info;
+  if (s == DVS_OK && p->expect_dim && p->expect_dim != in.dim)
+    s = fail(DVS_ERR_DIM, "RaBitQ artifact dim mismatch: expected " + std::to_string(p->expect_dim) + ", got " +
+                              std::to_string(in.dim));
+  if (s == DVS_OK && p->expect_bits && p->expect_bits != in.rabitq_bits)
+    s = fail(DVS_ERR_BITS, "RaBitQ artifact bits mismatch: expected " + std::to_string(p->expect_bits) + ", got " +
+                               std::to_string(in.rabitq_bits));
+  if (s == DVS_OK && p->expect_memory_nodes && p->expect_memory_nodes != in.num_memory_nodes)
+    s = fail(DVS_ERR_FORMAT, "RaBitQ artifact memory-node count mismatch: expected " +
+                                 std::to_string(p->expect_memory_nodes) + ", got " +
+                                 std::to_string(in.num_memory_nodes));
+  if (s == DVS_OK) {
+    ix->devs.resize(devs.size());
+    for (size_t i = 0; i < devs.size() && s == DVS_OK; ++i) {
+      ix->devs[i].ordinal = devs[i];
+      s = dvs::upload(ix->devs[i], ix->host);
+    }
+  }
+  if (s != DVS_OK) {
+    for (auto& d : ix->devs) d.release();
+    delete ix;
+    return s;
+  }
+  *out = ix;
+  return DVS_OK;
+}
+
+dvs_status dvs_close(dvs_index* ix) {
+  if (!ix) return fail(DVS_ERR_ARG, "null index");
+  for (auto& d : ix->devs) {
+    cudaSetDevice(d.ordinal);
+    if (d.stream) cudaStreamSynchronize(d.stream);
+    d.release();
+  }
+  delete ix;
+  return DVS_OK;
+}
+
+dvs_status dvs_index_get_info(const dvs_index* ix, dvs_index_info* out) {
+  if (!ix || !out) return fail(DVS_ERR_ARG, "null argument");
+  *out = ix->host.info;
+  return DVS_OK;
+}
+
+dvs_status dvs_set_hop_limit(dvs_index* ix, uint32_t max_expansions) {
+  if (!ix) return fail(DVS_ERR_ARG, "null index");
+  ix->hop_limit = max_expansions;
+  return DVS_OK;
+}
+
+dvs_status dvs_set_visited_slots(dvs_index* ix, uint32_t slots_per_beam_entry) {
+  if (!ix) return fail(DVS_ERR_ARG, "null index");
+  if (slots_per_beam_entry < 2 || slots_per_beam_entry > 256)
+    return fail(DVS_ERR_ARG, "visited slots per beam entry must be in 2..256");
+  std::lock_guard<std::mutex> g(ix->mu);
+  ix->slots_per_entry = slots_per_beam_entry;
+  return DVS_OK;
+}
+
+dvs_status dvs_index_download(const dvs_index* ix, uint32_t* h_adj, uint8_t* h_records, float* h_vecs,
+                              uint32_t* h_ids) {
+  if (!ix || ix->devs.empty()) return fail(DVS_ERR_ARG, "null index");
+  const dvs::Device& d = ix->devs[0];
+  const dvs::DevLayout& L = d.lay;
+  const uint64_t n = L.n;
+  DVS_CUDA(cudaSetDevice(d.ordinal));
+  if (h_adj) DVS_CUDA(cudaMemcpy(h_adj, d.adj, size_t(n) * L.R * 4, cudaMemcpyDeviceToHost));
+  if (h_ids) DVS_CUDA(cudaMemcpy(h_ids, d.ids, size_t(n) * 4, cudaMemcpyDeviceToHost));
+  if (h_vecs) {
+    std::vector<float> v(size_t(n) * L.vec_stride);
+    DVS_CUDA(cudaMemcpy(v.data(), d.vecs, v.size() * 4, cudaMemcpyDeviceToHost));
+    for (uint64_t g = 0; g < n; ++g) std::memcpy(h_vecs + g * L.dim, &v[g * L.vec_stride], size_t(L.dim) * 4);
+  }
+  if (h_records) {
+    const uint32_t packed = (L.bits * L.dim + 7) / 8, rs = packed + 8;
+    std::vector<uint32_t> r(size_t(n) * L.rec_words);
+    DVS_CUDA(cudaMemcpy(r.data(), d.rec, r.size() * 4, cudaMemcpyDeviceToHost));
+    for (uint64_t g = 0; g < n; ++g) {
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(r.data() + g * L.rec_words);
+      std::memcpy(h_records + g * rs, src, packed);
+      std::memcpy(h_records + g * rs + packed, src + size_t(L.code_words) * 4, 8);
+    }
+  }
+  return DVS_OK;
+}
+
+dvs_status dvs_search_device(dvs_index* ix, uint32_t slot, const float* d_queries, uint32_t nq, uint32_t dim,
+                             uint32_t k, uint32_t L, dvs_mode mode, uint32_t* d_out_ids, float* d_out_dist,
+                             uint32_t* d_counters, void* stream) {
+  dvs_status s = dvs::check_query_args(ix, nq, dim, k, L, mode);
+  if (s != DVS_OK) return s;
+  if (slot >= ix->devs.size()) return fail(DVS_ERR_ARG, "device slot out of range");
+  if (nq == 0) return DVS_OK;
+  if (!d_queries || !d_out_ids || !d_out_dist) return fail(DVS_ERR_ARG, "null buffer");
+  std::lock_guard<std::mutex> g(ix->mu);
+  dvs::Device& d = ix->devs[slot];
+  DVS_CUDA(cudaSetDevice(d.ordinal));
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : d.stream;
+  return dvs::search_on(ix, d, d_queries, nq, k, L, mode, d_out_ids, d_out_dist, d_counters, st, false);
+}
+
+dvs_status dvs_search(dvs_index* ix, const float* h_queries, uint32_t nq, uint32_t dim, uint32_t k, uint32_t L,
+                      dvs_mode mode, uint32_t* h_out_ids, float* h_out_dist, dvs_stats* stats) {
+  dvs_status s = dvs::check_query_args(ix, nq, dim, k, L, mode);
+  if (s != DVS_OK) return s;
+  if (stats) *stats = dvs_stats{};
+  if (nq == 0) return DVS_OK;
+  if (!h_queries || !h_out_ids || !h_out_dist) return fail(DVS_ERR_ARG, "null buffer");
+  for (size_t i = 0; i < size_t(nq) * dim; ++i)
+    if (!std::isfinite(h_queries[i])) return fail(DVS_ERR_ARG, "query contains a non-finite value");
+  std::lock_guard<std::mutex> g(ix->mu);
+  const size_t nd = ix->devs.size();
+  std::vector<dvs_status> st(nd, DVS_OK);
+  std::vector<std::string> msg(nd);
+  std::vector<dvs_stats> part(nd);
+  auto run = [&](size_t i) {
+    dvs::Device& d = ix->devs[i];
+    const size_t q0 = nq * i / nd, q1 = nq * (i + 1) / nd, m = q1 - q0;
+    if (m == 0) return;
+    auto body = [&]() -> dvs_status {
+      DVS_CUDA(cudaSetDevice(d.ordinal));
+      dvs_status r = dvs::ensure_scratch(d, m, k, true);
+      if (r != DVS_OK) return r;
+      DVS_CUDA(cudaMemcpyAsync(d.queries, h_queries + q0 * dim, m * dim * 4, cudaMemcpyHostToDevice, d.stream));
+      r = dvs::search_on(ix, d, d.queries, uint32_t(m), k, L, mode, d.out_ids, d.out_dist, d.counters, d.stream, true);
+      if (r != DVS_OK) return r;
+      DVS_CUDA(cudaMemcpyAsync(h_out_ids + q0 * k, d.out_ids, m * k * 4, cudaMemcpyDeviceToHost, d.stream));
+      DVS_CUDA(cudaMemcpyAsync(h_out_dist + q0 * k, d.out_dist, m * k * 4, cudaMemcpyDeviceToHost, d.stream));
+      std::vector<uint32_t> cnt(m * 4);
+      uint32_t work[4] = {0, 0, 0, 0};
+      DVS_CUDA(cudaMemcpyAsync(cnt.data(), d.counters, m * 16, cudaMemcpyDeviceToHost, d.stream));
+      DVS_CUDA(cudaMemcpyAsync(work, d.work, 16, cudaMemcpyDeviceToHost, d.stream));
+      DVS_CUDA(cudaStreamSynchronize(d.stream));
+      float ms = 0.f;
+      DVS_CUDA(cudaEventElapsedTime(&ms, d.ev0, d.ev1));
+      dvs_stats& ps = part[i];
+      for (size_t q = 0; q < m; ++q) {
+        ps.expansions += cnt[q * 4 + 0];
+        ps.estimates += cnt[q * 4 + 1];
+        ps.reranked += cnt[q * 4 + 2];
+      }
+      ps.overflow_queries = work[2];
+      ps.device_ms = ms;
+      if (work[1] & dvs::kErrCapacity)
+        return fail(DVS_ERR_CAPACITY, "a query's visited set exceeded its capacity; its results are partial");
+      if (work[1] & dvs::kErrHopLimit)
+        return fail(DVS_ERR_HOP_LIMIT, "a query reached the expansion limit; its results are partial");
+      return DVS_OK;
+    };
+    st[i] = body();
+    if (st[i] != DVS_OK) msg[i] = dvs_last_error();
+  };
+  if (nd == 1) {
+    run(0);
+  } else {
+    std::vector<std::thread> th;
+    for (size_t i = 0; i < nd; ++i) th.emplace_back(run, i);
+    for (auto& t : th) t.join();
+  }
+  for (size_t i = 0; i < nd; ++i) {
+    if (stats) {
+      stats->expansions += part[i].expansions;
+      stats->estimates += part[i].estimates;
+      stats->reranked += part[i].reranked;
+      stats->overflow_queries += part[i].overflow_queries;
+      stats->device_ms = std::max(stats->device_ms, part[i].device_ms);
+    }
+  }
+  for (size_t i = 0; i < nd; ++i)
+    if (st[i] != DVS_OK) return fail(st[i], msg[i]);
+  return DVS_OK;
+}
+
+dvs_status dvs_query_prepare(const float* d_query, const float* d_P, const float* d_centroid, float* d_rot_query,
+                             float* d_factor, uint32_t nq, uint32_t dim, uint32_t bits, void* stream) {
+  if (!d_query || !d_P || !d_centroid || !d_rot_query || !d_factor) return fail(DVS_ERR_ARG, "null buffer");
+  if (bits != 1 && bits != 2 && bits != 4 && bits != 8) return fail(DVS_ERR_BITS, "bits must be 1, 2, 4, or 8");
+  if (dim == 0) return fail(DVS_ERR_DIM, "dim must be > 0");
+  DVS_CUDA(dvs::launch_prepare(d_query, dim, d_P, d_centroid, d_rot_query, dim, d_factor, 3, dim, bits, nq,
+                               static_cast<cudaStream_t>(stream)));
+  return DVS_OK;
+}
+
+dvs_status dvs_rabitq_estimate(const float* d_rot_query, const float* d_factor, const uint8_t* d_records,
+                               float* d_dist, uint32_t n, uint32_t dim, uint32_t bits, void* stream) {
+  if (!d_rot_query || !d_factor || !d_records || !d_dist) return fail(DVS_ERR_ARG, "null buffer");
+  if (bits != 1 && bits != 2 && bits != 4)
+    return fail(DVS_ERR_BITS, "the estimator supports 1-, 2- and 4-bit codes; got " + std::to_string(bits));
+  DVS_CUDA(dvs::launch_estimate_ref_layout(d_rot_query, d_factor, d_records, d_dist, n, dim, bits,
+                                           static_cast<cudaStream_t>(stream)));
+  return DVS_OK;
+}
+
+dvs_status dvs_l2_distances(const float* d_query, const float* d_candidates, float* d_dist, uint32_t n, uint32_t dim,
+                            void* stream) {
+  if (!d_query || !d_candidates || !d_dist) return fail(DVS_ERR_ARG, "null buffer");
+  if (dim == 0) return fail(DVS_ERR_DIM, "dim must be > 0");
+  DVS_CUDA(dvs::launch_l2_rows(d_query, d_candidates, d_dist, n, dim, static_cast<cudaStream_t>(stream)));
+  return DVS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,179 @@
+// Device arithmetic shared by the kernels.  Every routine fixes the order of its
+// floating-point operations (explicit __f*_rn intrinsics, so nvcc cannot
+// re-contract them) to the order the reference's kernels use, which the CPU
+// oracle restates; results are therefore identical bit for bit.
+#pragma once
+
+#include <cfloat>
+#include <cstdint>
+
+namespace dvs {
+
+constexpr uint32_t kEmptySlot = 0xFFFFFFFFu;
+constexpr uint32_t kExpandedBit = 0x80000000u;
+
+__device__ __forceinline__ float tile4_sum(float s0, float s1, float s2, float s3) {
+  // cg::reduce over a 4-lane tile: xor 2, then xor 1.
+  return __fadd_rn(__fadd_rn(s0, s2), __fadd_rn(s1, s3));
+}
+
+// Reduce the 4 lanes of an aligned lane quad with the same butterfly; every lane
+// of the quad receives the tile sum.
+__device__ __forceinline__ float quad_butterfly(float v) {
+  v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+  v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+  return v;
+}
+
+// Small non-negative integer (< 2^23) to float, exact, without the conversion unit.
+__device__ __forceinline__ float small_u2f(uint32_t x) {
+  return __fsub_rn(__uint_as_float(0x4B000000u | x), 8388608.0f);
+}
+
+// One lane's share of batch_l2_squared_distance_kernel<4>
+// (src/gpu/kernels/distance_kernels.cuh:38-81): lane t of the quad walks float4
+// chunks t, t+4, ... then tail dim n4*4+t.  `q` and `x` are 16-byte aligned.
+__device__ __forceinline__ float l2_quad_partial(const float* __restrict__ q, const float* __restrict__ x,
+                                                 uint32_t dim, uint32_t t) {
+  const uint32_t n4 = dim >> 2;
+  const float4* q4 = reinterpret_cast<const float4*>(q);
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  float acc = 0.f;
+  uint32_t i = t;
+  // four chunks per trip keep four independent loads in flight
+  for (; i + 12 < n4; i += 16) {
+    const float4 a0 = __ldg(x4 + i), a1 = __ldg(x4 + i + 4), a2 = __ldg(x4 + i + 8), a3 = __ldg(x4 + i + 12);
+    const float4 b0 = q4[i], b1 = q4[i + 4], b2 = q4[i + 8], b3 = q4[i + 12];
+#define DVS_ACC4(B, A)                                   \
+  {                                                      \
+    float d;                                             \
+    d = __fsub_rn(B.x, A.x); acc = __fmaf_rn(d, d, acc); \
+    d = __fsub_rn(B.y, A.y); acc = __fmaf_rn(d, d, acc); \
+    d = __fsub_rn(B.z, A.z); acc = __fmaf_rn(d, d, acc); \
+    d = __fsub_rn(B.w, A.w); acc = __fmaf_rn(d, d, acc); \
+  }
+    DVS_ACC4(b0, a0) DVS_ACC4(b1, a1) DVS_ACC4(b2, a2) DVS_ACC4(b3, a3)
+  }
+  for (; i < n4; i += 4) {
+    const float4 a = __ldg(x4 + i);
+    const float4 b = q4[i];
+    DVS_ACC4(b, a)
+  }
+#undef DVS_ACC4
+  const uint32_t tail = (n4 << 2) + t;
+  if (tail < dim) {
+    const float d = __fsub_rn(q[tail], __ldg(x + tail));
+    acc = __fmaf_rn(d, d, acc);
+  }
+  return acc;
+}
+
+// Same chain order on a single thread (all four lanes' chains), for callers that
+// give one thread a whole row.
+__device__ __forceinline__ float l2_single(const float* __restrict__ q, const float* __restrict__ x, uint32_t dim) {
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t n4 = dim >> 2;
+  for (uint32_t i = 0; i < n4; ++i) {
+    float& a = s[i & 3];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float d = __fsub_rn(q[4 * i + k], x[4 * i + k]);
+      a = __fmaf_rn(d, d, a);
+    }
+  }
+  for (uint32_t i = n4 << 2; i < dim; ++i) {
+    const float d = __fsub_rn(q[i], x[i]);
+    float& a = s[(i - (n4 << 2)) & 3];
+    a = __fmaf_rn(d, d, a);
+  }
+  return tile4_sum(s[0], s[1], s[2], s[3]);
+}
+
+// RaBitQ estimate from the four chain sums (distance_kernels.cuh:132-136 as nvcc
+// contracts it): add_o + q.add + rescale_o * (dot + k1xSumq * (2^B - 1)).
+__device__ __forceinline__ float rabitq_finish(float dot, float add_o, float rescale_o, float q_add, float q_k1,
+                                               float k1) {
+  return __fmaf_rn(rescale_o, __fmaf_rn(q_k1, k1, dot), __fadd_rn(add_o, q_add));
+}
+
+// Accumulates one 32-bit word of packed B-bit codes (B in {1,2,4}) that covers
+// dims [j0, j0 + 32/B) into the four chains (dim j -> chain j & 3).  `qr` is the
+// rotated query in shared memory.
+template <int BITS>
+__device__ __forceinline__ void rabitq_word(uint32_t word, const float* __restrict__ qr, uint32_t j0, uint32_t dim,
+                                            float& s0, float& s1, float& s2, float& s3) {
+  constexpr int kPer = 32 / BITS;
+  constexpr uint32_t kMask = (1u << BITS) - 1u;
+  if (j0 + kPer <= dim) {
+#pragma unroll
+    for (int n = 0; n < kPer; n += 4) {
+      const float4 qv = *reinterpret_cast<const float4*>(qr + j0 + n);
+      s0 = __fmaf_rn(small_u2f((word >> (BITS * (n + 0))) & kMask), qv.x, s0);
+      s1 = __fmaf_rn(small_u2f((word >> (BITS * (n + 1))) & kMask), qv.y, s1);
+      s2 = __fmaf_rn(small_u2f((word >> (BITS * (n + 2))) & kMask), qv.z, s2);
+      s3 = __fmaf_rn(small_u2f((word >> (BITS * (n + 3))) & kMask), qv.w, s3);
+    }
+  } else {
+    for (int n = 0; n < kPer && j0 + n < dim; ++n) {
+      const float val = small_u2f((word >> (BITS * n)) & kMask);
+      const float qv = qr[j0 + n];
+      switch (n & 3) {
+        case 0: s0 = __fmaf_rn(val, qv, s0); break;
+        case 1: s1 = __fmaf_rn(val, qv, s1); break;
+        case 2: s2 = __fmaf_rn(val, qv, s2); break;
+        default: s3 = __fmaf_rn(val, qv, s3); break;
+      }
+    }
+  }
+}
+
+// Medoid seed distance (L2Distance / IPDistance on the host in the reference,
+// src/common/distance.hh:80-159): eight AVX lanes over 16-float chunks, a
+// left-to-right horizontal sum, then the tail.  Lanes 0..7 of the warp each own
+// one AVX lane; the result is returned on every lane.
+__device__ __forceinline__ float seed_distance_warp(const float* __restrict__ q, const float* __restrict__ x,
+                                                    uint32_t dim, bool ip, uint32_t lane) {
+  const uint32_t q16 = dim >> 4 << 4;
+  float acc = 0.f;
+  if (lane < 8) {
+    for (uint32_t c = 0; c < q16; c += 16) {
+      const float a0 = q[c + lane], b0 = __ldg(x + c + lane);
+      const float a1 = q[c + 8 + lane], b1 = __ldg(x + c + 8 + lane);
+      if (ip) {
+        acc = __fmaf_rn(a0, b0, acc);
+        acc = __fmaf_rn(a1, b1, acc);
+      } else {
+        const float d0 = __fsub_rn(a0, b0);
+        acc = __fmaf_rn(d0, d0, acc);
+        const float d1 = __fsub_rn(a1, b1);
+        acc = __fmaf_rn(d1, d1, acc);
+      }
+    }
+  }
+  float r = __shfl_sync(0xFFFFFFFFu, acc, 0);
+#pragma unroll
+  for (int l = 1; l < 8; ++l) r = __fadd_rn(r, __shfl_sync(0xFFFFFFFFu, acc, l));
+  if (ip) {
+    float tail = 0.f;
+    for (uint32_t i = q16; i < dim; ++i) tail = __fmaf_rn(q[i], __ldg(x + i), tail);
+    return __fsub_rn(1.0f, __fadd_rn(r, tail));
+  }
+  for (uint32_t i = q16; i < dim; ++i) {
+    const float d = __fsub_rn(q[i], __ldg(x + i));
+    r = __fmaf_rn(d, d, r);
+  }
+  return r;
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm volatile("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+__device__ __forceinline__ uint32_t hash_slot(uint32_t id, uint32_t cap) {
+  const uint32_t h = id * 0x9E3779B1u;
+  return uint32_t((uint64_t(h) * cap) >> 32);
+}
+
+}  // namespace dvs

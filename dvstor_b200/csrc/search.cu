@@ -1,0 +1,508 @@
+// Query-path kernels for sm_100a.
+//
+// search_kernel: a persistent kernel in which every warp takes queries from an
+// atomic counter and runs the whole of Vamana::knn (src/vamana/vamana.hh:57-452)
+// for one query at a time, on device-resident adjacency, RaBitQ records and
+// vectors: medoid seed, beam expansion with a shared-memory visited set, RaBitQ
+// estimates (rabitq_gpu) or exact distances (exact_gpu), lower_bound insertion
+// into a beam of capacity L+64 (L), exact rerank of the whole beam and the final
+// ordering.  The reference does each expansion as an RDMA read, an H2D copy, a
+// tiny kernel launch and a blocking D2H copy (src/vamana/vamana.hh:131-356);
+// here an expansion is ~1 µs of on-chip work and two dependent HBM reads.
+//
+// Beam semantics reproduced exactly (ids match the oracle bit for bit):
+//   * a new candidate goes before every entry of equal distance
+//     (std::lower_bound in insert_into_beam, vamana.hh:1014-1030); of several
+//     equal new candidates of one expansion, the later-inserted comes first;
+//   * the beam is trimmed to its capacity after the insertions;
+//   * the next node to expand is the first unexpanded entry with distance
+//     < FLT_MAX (vamana.hh:134-141);
+//   * the visited set holds every neighbour ever seen (vamana.hh:174-182);
+//   * after the loop, rabitq_gpu replaces every beam distance by the exact L2
+//     (vamana.hh:358-422) and the beam is ordered by distance (vamana.hh:425);
+//     entries of equal distance keep beam order (std::sort leaves their order
+//     unspecified; this is the one documented tie).
+
+#include <cuda_runtime.h>
+
+#include "device_math.cuh"
+#include "search.cuh"
+
+namespace dvs {
+
+namespace {
+
+constexpr uint32_t kFull = 0xFFFFFFFFu;
+
+// Inserts `id` into a linear-probing table; true when it was not present.
+// The table never fills: callers keep its load under the limit.
+__device__ __forceinline__ bool table_insert(uint32_t* tab, uint32_t cap, uint32_t id) {
+  volatile uint32_t* vt = tab;
+  uint32_t s = hash_slot(id, cap);
+  for (uint32_t probe = 0; probe < cap; ++probe) {
+    const uint32_t cur = vt[s];
+    if (cur == id) return false;
+    if (cur == kEmptySlot) {
+      const uint32_t old = atomicCAS(tab + s, kEmptySlot, id);
+      if (old == kEmptySlot) return true;
+      if (old == id) return false;
+    }
+    s = (s + 1 == cap) ? 0 : s + 1;
+  }
+  return false;
+}
+
+__device__ __forceinline__ bool table_contains(const uint32_t* tab, uint32_t cap, uint32_t id) {
+  const volatile uint32_t* vt = tab;
+  uint32_t s = hash_slot(id, cap);
+  for (uint32_t probe = 0; probe < cap; ++probe) {
+    const uint32_t cur = vt[s];
+    if (cur == id) return true;
+    if (cur == kEmptySlot) return false;
+    s = (s + 1 == cap) ? 0 : s + 1;
+  }
+  return false;
+}
+
+// RaBitQ estimate of one record by one lane (all four chains on this lane).
+template <int BITS>
+__device__ __forceinline__ float estimate_lane(const DevLayout& ix, uint32_t c, const float* __restrict__ qr,
+                                               float q_add, float q_k1) {
+  constexpr int kPer = 32 / BITS;
+  const uint4* r = reinterpret_cast<const uint4*>(ix.rec) + size_t(c) * (ix.rec_words >> 2);
+  const uint32_t nch = (ix.code_words + 2 + 3) >> 2;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, add_o = 0.f, rs_o = 0.f;
+  for (uint32_t c0 = 0; c0 < nch; c0 += 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+      if (c0 + t < nch) v[t] = __ldg(r + c0 + t);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (c0 + t < nch) {
+        const uint32_t w[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t wi = (c0 + t) * 4 + e;
+          if (wi < ix.code_words)
+            rabitq_word<BITS>(w[e], qr, wi * kPer, ix.dim, s0, s1, s2, s3);
+          else if (wi == ix.code_words)
+            add_o = __uint_as_float(w[e]);
+          else if (wi == ix.code_words + 1)
+            rs_o = __uint_as_float(w[e]);
+        }
+      }
+    }
+  }
+  return rabitq_finish(tile4_sum(s0, s1, s2, s3), add_o, rs_o, q_add, q_k1, float((1u << BITS) - 1u));
+}
+
+// Exact L2 of `count` rows (slot ids in `rows`) against q, written to `out`;
+// 4 lanes per row, 8 rows per round.  Warp-uniform control flow.
+__device__ __forceinline__ void l2_rows_warp(const DevLayout& ix, const float* __restrict__ q,
+                                             const uint32_t* rows, uint32_t count, float* out, uint32_t lane,
+                                             uint32_t row_mask) {
+  const uint32_t t = lane & 3;
+  for (uint32_t r0 = 0; r0 < count; r0 += 8) {
+    const uint32_t i = r0 + (lane >> 2);
+    float part = 0.f;
+    if (i < count) {
+      const uint32_t row = rows[i] & row_mask;
+      part = l2_quad_partial(q, ix.vecs + size_t(row) * ix.vec_stride, ix.dim, t);
+    }
+    const float total = quad_butterfly(part);
+    if (i < count && t == 0) out[i] = total;
+  }
+}
+
+template <int BITS, int NPL>
+__global__ void __launch_bounds__(256) search_kernel(const SearchArgs a) {
+  extern __shared__ __align__(16) uint32_t smem[];
+  const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const DevLayout& ix = a.ix;
+  uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap);
+  float* bdA = reinterpret_cast<float*>(base);
+  uint32_t* biA = base + a.cap_pad;
+  float* bdB = reinterpret_cast<float*>(base + 2 * a.cap_pad);
+  uint32_t* biB = base + 3 * a.cap_pad;
+  float* qv = reinterpret_cast<float*>(base + 4 * a.cap_pad);
+  float* qr = qv + a.dim_pad;
+  uint32_t* cid = base + 4 * a.cap_pad + 2 * a.dim_pad;
+  float* cd = reinterpret_cast<float*>(cid + 64);
+  uint32_t* htab = cid + 128;
+  const uint32_t warp_slot = blockIdx.x * (blockDim.x >> 5) + wib;
+  uint32_t* gtab = a.ovf ? a.ovf + size_t(warp_slot) * a.ovf_cap : nullptr;
+  const bool rabitq = a.mode == 0;
+  const uint32_t dim = ix.dim, R = ix.R;
+
+  for (;;) {
+    uint32_t qi = 0;
+    if (lane == 0) qi = atomicAdd(a.work, 1u);
+    qi = __shfl_sync(kFull, qi, 0);
+    if (qi >= a.nq) break;
+
+    // ---- per-query set-up ----
+    for (uint32_t j = lane; j < a.dim_pad; j += 32) {
+      qv[j] = j < dim ? a.queries[size_t(qi) * dim + j] : 0.f;
+      qr[j] = rabitq ? a.qrot[size_t(qi) * ix.vec_stride + j] : 0.f;
+    }
+    float q_add = 0.f, q_k1 = 0.f;
+    if (rabitq) {
+      q_add = a.qfac[size_t(qi) * 4 + 0];
+      q_k1 = a.qfac[size_t(qi) * 4 + 1];
+    }
+    {
+      uint4* h4 = reinterpret_cast<uint4*>(htab);
+      const uint4 e = make_uint4(kEmptySlot, kEmptySlot, kEmptySlot, kEmptySlot);
+      for (uint32_t j = lane; j < (a.hcap >> 2); j += 32) h4[j] = e;
+    }
+    __syncwarp();
+    const float md = seed_distance_warp(qv, ix.vecs + size_t(ix.medoid) * ix.vec_stride, dim, ix.metric == 1, lane);
+    if (lane == 0) {
+      bdA[0] = md;
+      biA[0] = ix.medoid;
+      htab[hash_slot(ix.medoid, a.hcap)] = ix.medoid;
+    }
+    __syncwarp();
+    float* bd = bdA;
+    uint32_t* bi = biA;
+    float* bdo = bdB;
+    uint32_t* bio = biB;
+    uint32_t nb = 1, hcount = 1, gcount = 0, H = 0, E = 0, err = 0;
+    bool overflow = false;
+
+    for (;;) {
+      // ---- select the first unexpanded entry (vamana.hh:134-141) ----
+      int best = -1;
+      for (uint32_t b = 0; b < nb; b += 32) {
+        const uint32_t p = b + lane;
+        const bool ok = p < nb && !(bi[p] & kExpandedBit) && bd[p] < FLT_MAX;
+        const uint32_t m = __ballot_sync(kFull, ok);
+        if (m) {
+          best = int(b + __ffs(m) - 1);
+          break;
+        }
+      }
+      if (best < 0) break;
+      if (a.hop_limit && H >= a.hop_limit) {
+        err |= kErrHopLimit;
+        break;
+      }
+      const uint32_t u = bi[best];
+      __syncwarp();
+      if (lane == 0) bi[best] = u | kExpandedBit;
+      ++H;
+
+      // ---- neighbours, visited filter (vamana.hh:162-182) ----
+      uint32_t nbr[NPL];
+#pragma unroll
+      for (int s = 0; s < NPL; ++s) {
+        const uint32_t j = lane + 32u * s;
+        nbr[s] = j < R ? __ldg(ix.adj + size_t(u) * R + j) : kEmptySlot;
+      }
+      uint32_t m = 0;
+#pragma unroll
+      for (int s = 0; s < NPL; ++s) {
+        const uint32_t peers = __match_any_sync(kFull, nbr[s]);
+        const bool first = nbr[s] != kEmptySlot && (peers & lanemask_lt()) == 0;
+        if (!overflow && hcount + 32 > a.hlimit) {
+          overflow = gtab != nullptr;
+          if (!overflow) {
+            err |= kErrCapacity;
+          } else {
+            uint4* g4 = reinterpret_cast<uint4*>(gtab);
+            const uint4 e = make_uint4(kEmptySlot, kEmptySlot, kEmptySlot, kEmptySlot);
+            for (uint32_t j = lane; j < (a.ovf_cap >> 2); j += 32) g4[j] = e;
+            __syncwarp();
+          }
+        }
+        if (overflow && gcount + 32 > a.ovf_limit) err |= kErrCapacity;
+        if (err & kErrCapacity) break;
+        bool fresh = false;
+        if (first) {
+          if (!overflow)
+            fresh = table_insert(htab, a.hcap, nbr[s]);
+          else
+            fresh = !table_contains(htab, a.hcap, nbr[s]) && table_insert(gtab, a.ovf_cap, nbr[s]);
+        }
+        const uint32_t bal = __ballot_sync(kFull, fresh);
+        if (fresh) cid[m + __popc(bal & lanemask_lt())] = nbr[s];
+        const uint32_t cnt = __popc(bal);
+        m += cnt;
+        if (overflow)
+          gcount += cnt;
+        else
+          hcount += cnt;
+        __syncwarp();
+      }
+      if (err & kErrCapacity) break;
+      if (m == 0) continue;
+      E += m;
+
+      // ---- distances of the unvisited neighbours ----
+      if (rabitq) {
+        for (uint32_t i = lane; i < m; i += 32) cd[i] = estimate_lane<BITS>(ix, cid[i], qr, q_add, q_k1);
+      } else {
+        l2_rows_warp(ix, qv, cid, m, cd, lane, 0xFFFFFFFFu);
+      }
+      __syncwarp();
+
+      // ---- insert_into_beam for all m candidates (vamana.hh:347-352, 1014-1030) ----
+      const uint32_t nb_new = min(a.cap, nb + m);
+      for (uint32_t i = lane; i < m; i += 32) {
+        const float d = cd[i];
+        uint32_t r = 0;
+        for (uint32_t j = 0; j < m; ++j) {
+          const float dj = cd[j];
+          r += (dj < d) || (dj == d && j > i);
+        }
+        if (r >= a.cap) continue;
+        uint32_t lo = 0, hi = nb;
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          if (bd[mid] < d)
+            lo = mid + 1;
+          else
+            hi = mid;
+        }
+        const uint32_t pos = r + lo;
+        if (pos < a.cap) {
+          bdo[pos] = d;
+          bio[pos] = cid[i];
+        }
+      }
+      for (uint32_t p = lane; p < nb; p += 32) {
+        const float d = bd[p];
+        uint32_t c = 0;
+        for (uint32_t j = 0; j < m; ++j) c += cd[j] <= d;
+        const uint32_t pos = p + c;
+        if (pos < a.cap) {
+          bdo[pos] = d;
+          bio[pos] = bi[p];
+        }
+      }
+      __syncwarp();
+      float* tf = bd;
+      bd = bdo;
+      bdo = tf;
+      uint32_t* ti = bi;
+      bi = bio;
+      bio = ti;
+      nb = nb_new;
+    }
+
+    // ---- rerank (vamana.hh:358-422) and final order (vamana.hh:424-446) ----
+    uint32_t Cr = 0;
+    if (rabitq && nb > 0) {
+      __syncwarp();
+      l2_rows_warp(ix, qv, bi, nb, bd, lane, ~kExpandedBit);
+      Cr = nb;
+      __syncwarp();
+      for (uint32_t p = lane; p < nb; p += 32) {
+        const float d = bd[p];
+        uint32_t r = 0;
+        for (uint32_t q = 0; q < nb; ++q) {
+          const float dq = bd[q];
+          r += (dq < d) || (dq == d && q < p);
+        }
+        if (r < a.k) {
+          a.out_ids[size_t(qi) * a.k + r] = ix.ids[bi[p] & ~kExpandedBit];
+          a.out_dist[size_t(qi) * a.k + r] = d;
+        }
+      }
+    } else {
+      for (uint32_t p = lane; p < nb && p < a.k; p += 32) {
+        a.out_ids[size_t(qi) * a.k + p] = ix.ids[bi[p] & ~kExpandedBit];
+        a.out_dist[size_t(qi) * a.k + p] = bd[p];
+      }
+    }
+    for (uint32_t r = nb + lane; r < a.k; r += 32) {
+      a.out_ids[size_t(qi) * a.k + r] = kEmptySlot;
+      a.out_dist[size_t(qi) * a.k + r] = __int_as_float(0x7F800000);
+    }
+    if (lane == 0) {
+      if (a.counters) {
+        a.counters[size_t(qi) * 4 + 0] = H;
+        a.counters[size_t(qi) * 4 + 1] = E;
+        a.counters[size_t(qi) * 4 + 2] = Cr;
+        a.counters[size_t(qi) * 4 + 3] = min(nb, a.k) | (err << 16);
+      }
+      if (err) atomicOr(a.work + 1, err);
+      if (overflow) atomicAdd(a.work + 2, 1u);
+    }
+    __syncwarp();
+  }
+}
+
+// q' = P^T q in a fixed order (sequential fmaf over i) and the factors of
+// rabitq_query_prepare_kernel<4,B> (src/gpu/kernels/distance_kernels.cuh:470-501).
+__global__ void __launch_bounds__(128) prepare_kernel(const float* __restrict__ Q, uint32_t q_stride,
+                                                      const float* __restrict__ P, const float* __restrict__ c,
+                                                      float* __restrict__ qrot, uint32_t qrot_stride,
+                                                      float* __restrict__ qfac, uint32_t fac_stride, uint32_t dim,
+                                                      uint32_t nq, float c_b) {
+  extern __shared__ float sh[];
+  float* qs = sh;
+  float* rs = sh + dim;
+  for (uint32_t q = blockIdx.x; q < nq; q += gridDim.x) {
+    for (uint32_t j = threadIdx.x; j < dim; j += blockDim.x) qs[j] = Q[size_t(q) * q_stride + j];
+    __syncthreads();
+    for (uint32_t j = threadIdx.x; j < dim; j += blockDim.x) {
+      const float* col = P + size_t(j) * dim;
+      float acc = 0.f;
+      for (uint32_t i = 0; i < dim; ++i) acc = __fmaf_rn(__ldg(col + i), qs[i], acc);
+      rs[j] = acc;
+      qrot[size_t(q) * qrot_stride + j] = acc;
+    }
+    for (uint32_t j = dim + threadIdx.x; j < qrot_stride; j += blockDim.x) qrot[size_t(q) * qrot_stride + j] = 0.f;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const uint32_t lane = threadIdx.x;
+      float sq = 0.f, sm = 0.f;
+      if (lane < 4) {
+        for (uint32_t j = lane; j < dim; j += 4) {
+          const float diff = __fsub_rn(rs[j], __ldg(c + j));
+          sq = __fmaf_rn(diff, diff, sq);
+          sm = __fadd_rn(sm, rs[j]);
+        }
+      }
+      sq = quad_butterfly(sq);
+      sm = quad_butterfly(sm);
+      if (lane == 0) {
+        qfac[size_t(q) * fac_stride + 0] = sq;
+        qfac[size_t(q) * fac_stride + 1] = __fmul_rn(-0.5f, sm);
+        qfac[size_t(q) * fac_stride + 2] = __fmul_rn(c_b, sm);
+        if (fac_stride > 3) qfac[size_t(q) * fac_stride + 3] = 0.f;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// batch_rabitq_distance_kernel on the reference's staged layout (records back
+// to back, rabitq_size bytes each, factors possibly unaligned): one thread per
+// record, byte-wise reads, same chain order.
+__global__ void estimate_ref_kernel(const float* __restrict__ qr, const float* __restrict__ f3,
+                                    const uint8_t* __restrict__ rec, float* __restrict__ out, uint32_t n,
+                                    uint32_t dim, uint32_t bits) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t packed = (bits * dim + 7) / 8;
+  const uint8_t* r = rec + size_t(i) * (packed + 8);
+  const uint32_t mask = (1u << bits) - 1u;
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  for (uint32_t j = 0; j < dim; ++j) {
+    const uint32_t bit_idx = j * bits, byte_idx = bit_idx >> 3, bit_off = bit_idx & 7;
+    uint32_t chunk = r[byte_idx];
+    if (bit_off + bits > 8 && byte_idx + 1 < packed) chunk |= uint32_t(r[byte_idx + 1]) << 8;
+    s[j & 3] = __fmaf_rn(small_u2f((chunk >> bit_off) & mask), qr[j], s[j & 3]);
+  }
+  uint32_t a_bits = 0, r_bits = 0;
+  for (int b = 0; b < 4; ++b) {
+    a_bits |= uint32_t(r[packed + b]) << (8 * b);
+    r_bits |= uint32_t(r[packed + 4 + b]) << (8 * b);
+  }
+  out[i] = rabitq_finish(tile4_sum(s[0], s[1], s[2], s[3]), __uint_as_float(a_bits), __uint_as_float(r_bits), f3[0],
+                         f3[1], float((1u << bits) - 1u));
+}
+
+// batch_l2_squared_distance_kernel<4> on contiguous rows: 4 lanes per row.
+__global__ void l2_rows_kernel(const float* __restrict__ q, const float* __restrict__ cand, float* __restrict__ out,
+                               uint32_t n, uint32_t dim) {
+  const uint32_t gtid = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t row = gtid >> 2, t = gtid & 3;
+  float acc = 0.f;
+  if (row < n) {
+    const float* x = cand + size_t(row) * dim;
+    const uint32_t n4 = dim >> 2;
+    for (uint32_t i = t; i < n4; i += 4) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float d = __fsub_rn(q[4 * i + k], x[4 * i + k]);
+        acc = __fmaf_rn(d, d, acc);
+      }
+    }
+    const uint32_t tail = (n4 << 2) + t;
+    if (tail < dim) {
+      const float d = __fsub_rn(q[tail], x[tail]);
+      acc = __fmaf_rn(d, d, acc);
+    }
+  }
+  acc = quad_butterfly(acc);
+  if (row < n && t == 0) out[row] = acc;
+}
+
+template <int BITS, int NPL>
+cudaError_t set_attr(size_t smem) {
+  return cudaFuncSetAttribute(search_kernel<BITS, NPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+}
+
+template <int BITS, int NPL>
+cudaError_t occ(uint32_t wpb, size_t smem, int* bps) {
+  cudaError_t e = set_attr<BITS, NPL>(smem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(bps, search_kernel<BITS, NPL>, int(wpb * 32), smem);
+}
+
+}  // namespace
+
+cudaError_t launch_prepare(const float* queries, uint32_t q_stride, const float* P, const float* c_rot, float* qrot,
+                           uint32_t qrot_stride, float* qfac, uint32_t fac_stride, uint32_t dim, uint32_t bits,
+                           uint32_t nq, cudaStream_t stream) {
+  if (nq == 0) return cudaSuccess;
+  const float c_b = -static_cast<float>((1u << bits) - 1u) / 2.0f;
+  const uint32_t grid = nq < 65535u ? nq : 65535u;
+  prepare_kernel<<<grid, 128, 2 * dim * sizeof(float), stream>>>(queries, q_stride, P, c_rot, qrot, qrot_stride,
+                                                                  qfac, fac_stride, dim, nq, c_b);
+  return cudaGetLastError();
+}
+
+cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t wpb, size_t smem, int* bps) {
+  const bool two = R > 32;
+  switch (bits) {
+    case 1: return two ? occ<1, 2>(wpb, smem, bps) : occ<1, 1>(wpb, smem, bps);
+    case 2: return two ? occ<2, 2>(wpb, smem, bps) : occ<2, 1>(wpb, smem, bps);
+    case 4: return two ? occ<4, 2>(wpb, smem, bps) : occ<4, 1>(wpb, smem, bps);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_search(const SearchArgs& a, uint32_t wpb, uint32_t blocks, cudaStream_t stream) {
+  const size_t smem = size_t(wpb) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap) * 4;
+  const bool two = a.ix.R > 32;
+  const dim3 grid(blocks), block(wpb * 32);
+  switch (a.ix.bits) {
+    case 1:
+      if (two) search_kernel<1, 2><<<grid, block, smem, stream>>>(a);
+      else search_kernel<1, 1><<<grid, block, smem, stream>>>(a);
+      break;
+    case 2:
+      if (two) search_kernel<2, 2><<<grid, block, smem, stream>>>(a);
+      else search_kernel<2, 1><<<grid, block, smem, stream>>>(a);
+      break;
+    case 4:
+      if (two) search_kernel<4, 2><<<grid, block, smem, stream>>>(a);
+      else search_kernel<4, 1><<<grid, block, smem, stream>>>(a);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_estimate_ref_layout(const float* qrot, const float* f3, const uint8_t* records, float* out,
+                                       uint32_t n, uint32_t dim, uint32_t bits, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  estimate_ref_kernel<<<(n + 127) / 128, 128, 0, stream>>>(qrot, f3, records, out, n, dim, bits);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_l2_rows(const float* q, const float* cand, float* out, uint32_t n, uint32_t dim,
+                           cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const uint64_t threads = uint64_t(n) * 4;
+  l2_rows_kernel<<<uint32_t((threads + 255) / 256), 256, 0, stream>>>(q, cand, out, n, dim);
+  return cudaGetLastError();
+}
+
+}  // namespace dvs

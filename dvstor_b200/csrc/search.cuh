@@ -1,0 +1,69 @@
+// Launch-side view of the search kernels (shared by search.cu and api.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace dvs {
+
+// Device layout of one index copy (dense slot order).
+//   adj      n*R u32 slot ids, kEmptySlot fill (non-empty first)
+//   rec      n records of rec_words u32: [codes zero-padded to code_words words |
+//            f32 add | f32 rescale | zero pad to a 16-byte multiple]
+//   vecs     n rows of vec_stride floats (dim, zero-padded to a multiple of 4)
+//   ids      n u32 node ids as stored in the shards
+struct DevLayout {
+  const uint32_t* adj = nullptr;
+  const uint32_t* rec = nullptr;
+  const float* vecs = nullptr;
+  const uint32_t* ids = nullptr;
+  const float* P = nullptr;         // dim*dim column-major rotation
+  const float* c_rot = nullptr;     // rotated centroid
+  uint64_t n = 0;
+  uint32_t dim = 0, R = 0, bits = 0, medoid = 0, metric = 0;
+  uint32_t rec_words = 0, code_words = 0, vec_stride = 0;
+};
+
+struct SearchArgs {
+  DevLayout ix;
+  const float* queries = nullptr;   // nq*dim, row stride dim
+  const float* qrot = nullptr;      // nq*vec_stride rotated queries
+  const float* qfac = nullptr;      // nq*4 {add, k1xSumq, kBxSumq, 0}
+  uint32_t nq = 0, k = 0, L = 0, cap = 0, mode = 0, hop_limit = 0;
+  uint32_t* out_ids = nullptr;
+  float* out_dist = nullptr;
+  uint32_t* counters = nullptr;     // nq*4: H, E, C_r, count | error bits << 16
+  uint32_t* work = nullptr;         // [0] next query, [1] error bits, [2] overflowed queries
+  uint32_t* ovf = nullptr;          // per warp slot visited overflow tables
+  uint32_t ovf_cap = 0, ovf_limit = 0;
+  uint32_t hcap = 0, hlimit = 0;    // shared-memory visited table
+  uint32_t cap_pad = 0, dim_pad = 0;
+};
+
+constexpr uint32_t kErrCapacity = 1u;
+constexpr uint32_t kErrHopLimit = 2u;
+
+// Words of shared memory one warp of the search kernel uses.
+__host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap) {
+  return 4 * cap_pad + 2 * dim_pad + 128 + hcap;
+}
+
+cudaError_t launch_prepare(const float* queries, uint32_t q_stride, const float* P, const float* c_rot, float* qrot,
+                           uint32_t qrot_stride, float* qfac, uint32_t fac_stride, uint32_t dim, uint32_t bits,
+                           uint32_t nq, cudaStream_t stream);
+
+// Launches the persistent search kernel; warps_per_block and blocks come from
+// the caller's occupancy computation.
+cudaError_t launch_search(const SearchArgs& a, uint32_t warps_per_block, uint32_t blocks, cudaStream_t stream);
+
+// Occupancy helper: blocks per SM for `warps_per_block` warps with the given
+// per-warp shared memory; also sets the kernel's dynamic smem attribute.
+cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t warps_per_block, size_t smem_bytes, int* blocks_per_sm);
+
+cudaError_t launch_estimate_ref_layout(const float* qrot, const float* f3, const uint8_t* records, float* out,
+                                       uint32_t n, uint32_t dim, uint32_t bits, cudaStream_t stream);
+cudaError_t launch_l2_rows(const float* q, const float* cand, float* out, uint32_t n, uint32_t dim,
+                           cudaStream_t stream);
+
+}  // namespace dvs

@@ -1,0 +1,194 @@
+"""GPU parity of the whole query path (dvs_search through the C ABI) against the
+oracle's restatement of Vamana::knn on the same index files and queries: final
+distances bit for bit, ids bit for bit outside groups of exactly equal distance,
+and the per-query work counters (expansions H, estimates E, reranked rows C_r)
+exactly."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import assert_results_match, normalized_gaussian, uniform_int_data, write_oracle_index
+
+pytestmark = pytest.mark.gpu
+
+
+class Case:
+    def __init__(self, oracle, tmp, name, X, R, Lb, bits=4, M=1, metric="l2", seed=1234):
+        self.idx = oracle.build_index(X, R=R, L=Lb, bits=bits, seed=seed, metric=metric)
+        self.prefix = write_oracle_index(oracle, self.idx, os.path.join(tmp, name, "idx"), M)
+
+
+@pytest.fixture(scope="module")
+def cases(oracle, tmp_path_factory):
+    tmp = str(tmp_path_factory.mktemp("idx"))
+    return {
+        "int128": Case(oracle, tmp, "int128", uniform_int_data(4000, 128, 0), 32, 64),
+        "gauss96": Case(oracle, tmp, "gauss96", normalized_gaussian(5000, 96, 2), 32, 64),
+        "r48": Case(oracle, tmp, "r48", normalized_gaussian(3000, 64, 4), 48, 64),
+        "bits2": Case(oracle, tmp, "bits2", normalized_gaussian(2000, 40, 5), 16, 32, bits=2),
+        "bits1": Case(oracle, tmp, "bits1", normalized_gaussian(2000, 64, 6), 16, 32, bits=1),
+        "ragged": Case(oracle, tmp, "ragged", normalized_gaussian(1500, 30, 7), 16, 32),
+        "ip": Case(oracle, tmp, "ip", normalized_gaussian(2000, 48, 8), 16, 32, metric="ip"),
+        "shards": Case(oracle, tmp, "shards", uniform_int_data(3000, 32, 9), 24, 48, M=3),
+        "tiny": Case(oracle, tmp, "tiny", normalized_gaussian(12, 8, 10), 4, 8),
+    }
+
+
+def run_both(gpu, oracle, case, Q, k, L, mode="rabitq_gpu"):
+    idx = case.idx
+    with gpu.Index(case.prefix) as ix:
+        ids, d, st = ix.search(Q, k, L, mode, stats=True)
+    cap = L + 64 if mode == "rabitq_gpu" else L
+    o_ids, o_d, o_cnt, b_ids, b_d = idx.knn(Q, k, L, mode, beam_cap=cap)
+    return ids, d, st, o_ids, o_d, o_cnt, b_ids, b_d
+
+
+@pytest.mark.parametrize("name,L", [("int128", 64), ("gauss96", 64), ("gauss96", 128), ("r48", 100), ("bits2", 32),
+                                    ("bits1", 48), ("ragged", 40), ("ip", 32), ("shards", 64)])
+@pytest.mark.parametrize("mode", ["rabitq_gpu", "exact_gpu"])
+def test_search_matches_oracle(gpu, oracle, cases, name, L, mode):
+    case = cases[name]
+    d = case.idx.dim
+    Q = (uniform_int_data(300, d, 99) if name in ("int128", "shards") else normalized_gaussian(300, d, 99))
+    k = 10
+    ids, dist, st, o_ids, o_d, o_cnt, b_ids, b_d = run_both(gpu, oracle, case, Q, k, L, mode)
+    assert_results_match(ids, dist, o_ids, o_d, b_ids, b_d)
+    assert st["expansions"] == int(o_cnt[:, 0].sum())
+    assert st["estimates"] == int(o_cnt[:, 1].sum())
+    assert st["reranked"] == int(o_cnt[:, 2].sum())
+
+
+def test_k_larger_than_beam_and_index(gpu, oracle, cases):
+    case = cases["tiny"]
+    Q = normalized_gaussian(20, 8, 3)
+    ids, d, st, o_ids, o_d, o_cnt, b_ids, b_d = run_both(gpu, oracle, case, Q, 16, 16)
+    assert_results_match(ids, d, o_ids, o_d, b_ids, b_d)
+    for q in range(len(Q)):
+        c = int(o_cnt[q, 3])
+        assert c <= 12 and (ids[q, c:] == gpu.EMPTY).all() and np.isinf(d[q, c:]).all()
+
+
+def test_k_equals_beam_width_exact(gpu, oracle, cases):
+    case = cases["gauss96"]
+    Q = normalized_gaussian(64, 96, 5)
+    ids, d, st, o_ids, o_d, o_cnt, b_ids, b_d = run_both(gpu, oracle, case, Q, 32, 32, "exact_gpu")
+    assert_results_match(ids, d, o_ids, o_d, b_ids, b_d)
+
+
+def test_query_is_its_own_nearest_neighbour(gpu, cases):
+    case = cases["gauss96"]
+    with gpu.Index(case.prefix) as ix:
+        ids, d = ix.search(case.idx.X[:200], 10, 64)
+    assert (ids[:, 0] == np.arange(200)).mean() > 0.97
+
+
+def test_repeat_runs_are_identical_and_batches_independent(gpu, cases):
+    case = cases["int128"]
+    Q = uniform_int_data(500, 128, 3)
+    with gpu.Index(case.prefix) as ix:
+        a = ix.search(Q, 10, 64)
+        b = ix.search(Q, 10, 64)
+        c = ix.search(Q[123:124], 10, 64)
+        e = ix.search(Q[:0], 10, 64)
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[0][123:124], c[0])
+    assert e[0].shape == (0, 10)
+
+
+def test_overflow_path_is_exact(gpu, oracle, cases):
+    """Queries whose visited set spills from the shared-memory table to the
+    global-memory table return the same results (spill forced by shrinking the
+    shared-memory table to 2 slots per beam entry)."""
+    case = cases["gauss96"]
+    Q = normalized_gaussian(100, 96, 21)
+    with gpu.Index(case.prefix) as ix:
+        ix.set_visited_slots(2)
+        ids, d, st = ix.search(Q, 10, 64, stats=True)
+    o_ids, o_d, o_cnt, b_ids, b_d = case.idx.knn(Q, 10, 64, beam_cap=128)
+    assert st["overflow_queries"] == 100
+    assert_results_match(ids, d, o_ids, o_d, b_ids, b_d)
+    assert st["estimates"] == int(o_cnt[:, 1].sum())
+
+
+def test_hop_limit_reports_error(gpu, cases):
+    case = cases["gauss96"]
+    with gpu.Index(case.prefix) as ix:
+        ix.set_hop_limit(3)
+        with pytest.raises(gpu.DvsError) as e:
+            ix.search(normalized_gaussian(4, 96, 1), 10, 64)
+        assert e.value.name == "DVS_ERR_HOP_LIMIT"
+        ix.set_hop_limit(0)
+        ix.search(normalized_gaussian(4, 96, 1), 10, 64)
+
+
+def test_argument_errors(gpu, cases):
+    case = cases["gauss96"]
+    with gpu.Index(case.prefix) as ix:
+        for args, name in [((normalized_gaussian(2, 95, 1), 10, 64), "DVS_ERR_DIM"),
+                           ((normalized_gaussian(2, 96, 1), 10, 5), "DVS_ERR_ARG"),
+                           ((normalized_gaussian(2, 96, 1), 0, 64), "DVS_ERR_ARG")]:
+            with pytest.raises(gpu.DvsError) as e:
+                ix.search(*args)
+            assert e.value.name == name
+        bad = normalized_gaussian(2, 96, 1)
+        bad[1, 3] = np.nan
+        with pytest.raises(gpu.DvsError):
+            ix.search(bad, 10, 64)
+    with pytest.raises(gpu.DvsError) as e:
+        gpu.Index(case.prefix, expect_dim=64)
+    assert e.value.name == "DVS_ERR_DIM"
+    with pytest.raises(gpu.DvsError) as e:
+        gpu.Index(case.prefix, expect_bits=1)
+    assert e.value.name == "DVS_ERR_BITS"
+
+
+def test_device_search_with_torch_buffers(gpu, oracle, cases):
+    import torch
+
+    case = cases["gauss96"]
+    Q = normalized_gaussian(128, 96, 17)
+    with gpu.Index(case.prefix) as ix:
+        h_ids, h_d = ix.search(Q, 10, 64)
+        dq = torch.from_numpy(Q).cuda()
+        cnt = torch.zeros((128, 4), dtype=torch.int32, device="cuda")
+        d_ids, d_d = ix.search_device(dq, 10, 64, d_counters=cnt)
+        torch.cuda.synchronize()
+    np.testing.assert_array_equal(d_ids.cpu().numpy().view(np.uint32), h_ids)
+    np.testing.assert_array_equal(d_d.cpu().numpy(), h_d)
+    _, _, o_cnt = case.idx.knn(Q, 10, 64)
+    np.testing.assert_array_equal(cnt.cpu().numpy()[:, :3].astype(np.uint32), o_cnt[:, :3])
+
+
+def test_index_download_matches_files(gpu, cases):
+    case = cases["shards"]
+    with gpu.Index(case.prefix) as ix:
+        adj, rec, vec, ids = ix.download()
+    np.testing.assert_array_equal(adj, case.idx.adj)
+    np.testing.assert_array_equal(rec, case.idx.records)
+    np.testing.assert_array_equal(vec, case.idx.X)
+    np.testing.assert_array_equal(ids, np.arange(len(ids)))
+
+
+def test_compute_service_single_query(gpu, cases):
+    case = cases["gauss96"]
+    svc = gpu.ComputeService(case.prefix, search_mode="rabitq_gpu", beam_width=64, k=10)
+    out = svc.search(case.idx.X[7], 10)
+    assert out[0] == 7 and len(out) == 10
+
+
+def test_plumbing_workload_parity(gpu, oracle, tmp_path):
+    """The CPU-runnable plumbing workload: 10,000 x 128 uniform-int vectors
+    (seed 0), 1,000 queries (seed 1), R=32, build L=128, 4-bit, k=10, L=64."""
+    X = uniform_int_data(10000, 128, 0)
+    Q = uniform_int_data(1000, 128, 1)
+    case = Case(oracle, str(tmp_path), "cfg1", X, 32, 128)
+    ids, d, st, o_ids, o_d, o_cnt, b_ids, b_d = run_both(gpu, oracle, case, Q, 10, 64)
+    ties = assert_results_match(ids, d, o_ids, o_d, b_ids, b_d)
+    assert st["expansions"] == int(o_cnt[:, 0].sum()) and st["estimates"] == int(o_cnt[:, 1].sum())
+    Xd, Qd = X.astype(np.float64), Q.astype(np.float64)
+    d2 = (Qd ** 2).sum(1)[:, None] - 2 * Qd @ Xd.T + (Xd ** 2).sum(1)[None]  # exact for integer data
+    gt = np.argsort(d2, 1, kind="stable")[:, :10]
+    recall = np.mean([len(set(ids[i]) & set(gt[i])) / 10 for i in range(len(Q))])
+    o_recall = np.mean([len(set(o_ids[i]) & set(gt[i])) / 10 for i in range(len(Q))])
+    assert abs(recall - o_recall) <= ties / (10 * len(Q)) + 1e-12
