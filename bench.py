@@ -1,0 +1,424 @@
+#!/usr/bin/env python
+"""Throughput of the rabitq_gpu query path: queries/sec at fixed beam width and k.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (default): 1,000,000 x 96 fp32 vectors, i.i.d. N(0,1) then
+L2-normalised (seed 2); Vamana R=32, build L=128, RaBitQ 4-bit; search k=10,
+beam L=64.  One step = one batch of 10,000 queries (same distribution) searched
+by one persistent kernel per GPU; with N GPUs every rank holds a replica of the
+index and searches its own 10,000-query batch per step (weak scaling, no
+collective on the data path).  The index (0.58 GB of adjacency, records and
+vectors) is larger than L2, which is not flushed between steps.
+
+`value`   device-resident queries -> device results (CUDA events, max over ranks).
+`e2e`     the public host API (dvs_search): pinned host queries in, host ids and
+          distances out, copies inside the timed region (wall clock per rank, max
+          over ranks).
+`--impl reference` times the reference's CPU Vamana beam search (restated in
+oracle/, the reference's own code cannot be built here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = "gauss-1m-d96"
+BATCH = 10_000
+PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "search_kernel_gauss-1m-d96.txt")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default=WORKLOAD)
+    ap.add_argument("--beam-width", type=int, default=None)
+    ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--cache", default=os.environ.get("DVS_BENCH_CACHE", "/tmp/dvs_b200_bench"))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+class Dist:
+    """torch.distributed plumbing when launched by torchrun."""
+
+    def __init__(self, backend):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+
+        dev = f"cuda:{self.local}" if self.pg.get_backend() == "nccl" else "cpu"
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def workload_params(name):
+    from dvstor_b200 import datasets
+
+    gen, n, dim, seed, R, build_L, search_L, k = datasets.WORKLOADS[name]
+    return dict(gen=gen, n=n, dim=dim, seed=seed, R=R, build_L=build_L, search_L=search_L, k=k)
+
+
+def index_prefix(args, wp):
+    tag = f"{args.workload}_R{wp['R']}_L{wp['build_L']}_b4_s1234"
+    return os.path.join(args.cache, tag, "idx")
+
+
+def ensure_index(args, wp, device, dist):
+    """Builds the index once per box (GPU builder) into the cache directory."""
+    from dvstor_b200 import datasets
+    from dvstor_b200.builder import build_index
+
+    prefix = index_prefix(args, wp)
+    done = prefix + ".done"
+    if dist.local == 0 and not os.path.exists(done):
+        t = time.time()
+        X = wp["gen"](wp["n"], wp["dim"], wp["seed"])
+        log(f"[bench] generated {X.shape} in {time.time() - t:.1f}s; building index on cuda:{device}")
+        t = time.time()
+        st = build_index(X, prefix, R=wp["R"], beam_width=wp["build_L"], alpha=1.2, rabitq_bits=4, seed=1234,
+                         device=device)
+        log(f"[bench] built in {time.time() - t:.1f}s ({st})")
+        open(done, "w").write(json.dumps(st))
+    dist.barrier()
+    return prefix
+
+
+def clocks_sampler(device):
+    """nvidia-smi clock/throttle sampling during the timed region."""
+    q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+    try:
+        p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-i", str(device),
+                              "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except OSError:
+        return None
+    lines = []
+    th = threading.Thread(target=lambda: lines.extend(p.stdout), daemon=True)
+    th.start()
+    return p, lines, th
+
+
+def clocks_summary(sampler):
+    if sampler is None:
+        return None
+    p, lines, th = sampler
+    p.terminate()
+    try:
+        p.wait(timeout=5)
+    except subprocess.TimeoutExpired:
+        p.kill()
+    th.join(timeout=2)
+    sm, mx, reasons = [], [], set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for ln in lines:
+        f = [x.strip() for x in ln.split(",")]
+        if len(f) < 9:
+            continue
+        try:
+            sm.append(float(f[1]))
+            mx.append(float(f[2]))
+        except ValueError:
+            continue
+        for nm, v in zip(names, f[5:9]):
+            if v.lower() == "active":
+                reasons.add(nm)
+    if not sm:
+        return None
+    return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def ground_truth(X, Q, k, device):
+    """Exact top-k by brute force on the GPU (fp32, TF32 off), chunked over queries."""
+    import torch
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    dev = torch.device(f"cuda:{device}")
+    Xt = torch.from_numpy(X).to(dev)
+    xx = (Xt.double() ** 2).sum(1).float()
+    out = []
+    for s in range(0, len(Q), 256):
+        q = torch.from_numpy(Q[s:s + 256]).to(dev)
+        d = xx[None, :] - 2.0 * (q @ Xt.T)
+        out.append(torch.topk(d, k, dim=1, largest=False).indices.cpu().numpy())
+    del Xt
+    torch.cuda.empty_cache()
+    return np.concatenate(out)
+
+
+def recall(ids, gt):
+    k = gt.shape[1]
+    return float(np.mean([len(set(ids[i][:k].tolist()) & set(gt[i].tolist())) / k for i in range(len(gt))]))
+
+
+def bytes_per_query(dim, R, bits, k, H, E, Cr, nq):
+    """Algorithmic bytes of one query: query row, H adjacency rows (R ids + count),
+    E RaBitQ records (codes + add + rescale), C_r rerank rows, the rotation
+    matrix amortised over the batch, and k (id, distance) results."""
+    s_code = (bits * dim + 7) // 8 + 8
+    return 4 * dim + H * (4 * R + 1) + E * s_code + Cr * 4 * dim + 4 * dim * dim / nq + 8 * k
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the search kernel from the committed ncu summary."""
+    try:
+        for ln in open(PROFILE_SUMMARY):
+            if ln.startswith("traffic_bytes_per_launch_full_workload="):
+                return float(ln.split("=", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def hbm_peak():
+    try:
+        return float(json.load(open(PEAKS))["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def cpu_baseline(idx_or, Q, L, k, target_s, gt_q=None):
+    """The reference's CPU beam search over a bounded query sample, all host threads."""
+    from oracle import oracle as O
+
+    cores = os.cpu_count() or 1
+    probe = Q[:min(len(Q), 2000)]
+    t = time.perf_counter()
+    O.cpu_beam_search_batch(idx_or.X, idx_or.adj, idx_or.medoid, probe, L, k, threads=cores)
+    qps0 = len(probe) / (time.perf_counter() - t)
+    n = int(min(len(Q), max(len(probe), qps0 * target_s)))
+    sample = Q[:n]
+    t = time.perf_counter()
+    ids, _ = O.cpu_beam_search_batch(idx_or.X, idx_or.adj, idx_or.medoid, sample, L, k, threads=cores)
+    el = time.perf_counter() - t
+    rec = recall(ids, gt_q) if gt_q is not None else None
+    return {"value": n / el, "unit": "queries/s", "cores": cores, "kind": "port",
+            "sample": f"{n} queries of the workload, beam_search (exact L2, L={L}) per query, "
+                      f"{cores} threads, {el:.1f}s", "recall_at_10": rec}
+
+
+def run_reference(args):
+    dist = Dist("gloo")
+    if dist.rank != 0:
+        dist.close()
+        return
+    from dvstor_b200 import datasets
+    from oracle import oracle as O
+
+    wp = workload_params(args.workload)
+    L = args.beam_width or wp["search_L"]
+    dist_single = Dist.__new__(Dist)
+    dist_single.world, dist_single.rank, dist_single.local, dist_single.pg = 1, 0, 0, None
+    prefix = ensure_index(args, wp, 0, dist_single)
+    idx = O.read_index(prefix)
+    cores = os.cpu_count() or 1
+    Qpool = datasets.queries_for(args.workload, 200_000, stream=0)
+    t = time.perf_counter()
+    O.cpu_beam_search_batch(idx.X, idx.adj, idx.medoid, Qpool[:1000], L, args.k, threads=cores)
+    qps0 = 1000 / (time.perf_counter() - t)
+    per_step = int(min(len(Qpool), max(1000, qps0 * 8.0)))  # ~8 s of CPU work per step
+    for s in range(args.warmup):
+        O.cpu_beam_search_batch(idx.X, idx.adj, idx.medoid, Qpool[:min(per_step, 2000)], L, args.k, threads=cores)
+    times = []
+    for s in range(args.steps):
+        q = np.roll(Qpool, -s * 997, axis=0)[:per_step]
+        t = time.perf_counter()
+        O.cpu_beam_search_batch(idx.X, idx.adj, idx.medoid, q, L, args.k, threads=cores)
+        times.append(time.perf_counter() - t)
+    qps = per_step * len(times) / sum(times)
+    gt = ground_truth(idx.X, Qpool[:1000], args.k, 0)
+    ids, _ = O.cpu_beam_search_batch(idx.X, idx.adj, idx.medoid, Qpool[:1000], L, args.k, threads=cores)
+    line = {
+        "impl": "reference", "metric": f"queries/sec at recall@10 parity (k={args.k}, L={L})", "value": qps,
+        "unit": "queries/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"], "build_L": wp["build_L"],
+                   "rabitq_bits": 4, "k": args.k, "beam_width": L, "queries_per_step": per_step,
+                   "l2": "index larger than L2, not flushed"},
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port",
+                         "sample": f"{per_step} queries per step, the reference's CPU beam_search restated "
+                                   f"(tools/vamana_offline_builder.cc:523-625), {cores} threads"},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "recall_at_10": recall(ids, gt),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+
+    dist = Dist("nccl")
+    device = dist.local
+    torch.cuda.set_device(device)
+    import dvstor_b200 as D
+    from dvstor_b200 import datasets
+
+    wp = workload_params(args.workload)
+    L = args.beam_width or wp["search_L"]
+    k = args.k
+    B = args.batch
+    prefix = ensure_index(args, wp, device, dist)
+    ix = D.Index(prefix, devices=(device,))
+    info = ix.info
+    nsteps = args.warmup + args.steps
+    Qpool = datasets.queries_for(args.workload, B * nsteps, stream=dist.rank)
+    dq = torch.from_numpy(Qpool).to(f"cuda:{device}").view(nsteps, B, wp["dim"])
+    out_ids = torch.empty((B, k), dtype=torch.int32, device=f"cuda:{device}")
+    out_d = torch.empty((B, k), dtype=torch.float32, device=f"cuda:{device}")
+    cnt = torch.zeros((B, 4), dtype=torch.int32, device=f"cuda:{device}")
+    stream = torch.cuda.Stream(device=device)
+
+    # ---- device-resident timed region ----
+    with torch.cuda.stream(stream):
+        for s in range(args.warmup):
+            ix.search_device(dq[s], k, L, d_out_ids=out_ids, d_out_dist=out_d, d_counters=cnt, stream=stream)
+    torch.cuda.synchronize(device)
+    ix.set_kernel_timing(True)
+    ix.kernel_times()
+    dist.barrier()
+    torch.cuda.synchronize(device)
+    sampler = clocks_sampler(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.steps):
+        ix.search_device(dq[args.warmup + s], k, L, d_out_ids=out_ids, d_out_dist=out_d, d_counters=cnt,
+                         stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    clocks = clocks_summary(sampler)
+    ms = e0.elapsed_time(e1)
+    n_search, prep_ms, search_ms = ix.kernel_times()
+    ix.set_kernel_timing(False)
+    ms_max = dist.max(ms)
+    value = dist.world * B * args.steps / (ms_max / 1e3)
+
+    # per-query work of the last step -> algorithmic bytes
+    c = cnt.cpu().numpy().astype(np.int64)
+    H, E, Cr = c[:, 0].mean(), c[:, 1].mean(), c[:, 2].mean()
+    bq = bytes_per_query(info.dim, info.R, info.rabitq_bits, k, H, E, Cr, B)
+    search_avg_ms = search_ms / max(n_search, 1)
+    achieved = bq * B / (search_avg_ms / 1e3) / 1e9
+    peak, peak_kind = hbm_peak()
+    tr = profile_traffic()
+
+    # ---- end to end through the host API ----
+    hq = torch.empty((B, wp["dim"]), dtype=torch.float32, pin_memory=True)
+    h_ids = torch.empty((B, k), dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
+    h_d = torch.empty((B, k), dtype=torch.float32, pin_memory=True).numpy()
+    hq_np = hq.numpy()
+    from dvstor_b200._lib import check, lib, ptr
+
+    def host_search(q):
+        hq_np[:] = q
+        check(lib().dvs_search(ix._h, ptr(hq_np), B, wp["dim"], k, L, 0, ptr(h_ids), ptr(h_d), None))
+
+    for s in range(min(args.warmup, 2)):
+        host_search(Qpool[s * B:(s + 1) * B])
+    dist.barrier()
+    e2e_times = []
+    for s in range(args.steps):
+        q = Qpool[((args.warmup + s) % nsteps) * B:((args.warmup + s) % nsteps + 1) * B]
+        t = time.perf_counter()
+        host_search(q)
+        e2e_times.append(time.perf_counter() - t)
+    e2e_s = dist.max(sum(e2e_times))
+    e2e = dist.world * B * args.steps / e2e_s
+
+    # ---- recall and the CPU baseline (rank 0) ----
+    rec = cpu = None
+    if dist.rank == 0:
+        from oracle import oracle as O
+
+        X = O.read_index(prefix) if not args.no_cpu_baseline else None
+        Xv = X.X if X is not None else ix.download()[2]
+        gtq = Qpool[:1000]
+        ix.search(gtq, k, L)
+        g_ids, _ = ix.search(gtq, k, L)
+        gt = ground_truth(Xv, gtq, k, device)
+        rec = recall(g_ids, gt)
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline(X, np.concatenate([gtq, Qpool[1000:]]), L, k, args.cpu_seconds, gt_q=None)
+            ids_cpu, _ = O.cpu_beam_search_batch(X.X, X.adj, X.medoid, gtq, L, k)
+            cpu["recall_at_10"] = recall(ids_cpu, gt)
+    ix.close()
+    if dist.rank == 0:
+        line = {
+            "metric": f"queries/sec at recall@10 parity (k={k}, L={L})", "value": value, "unit": "queries/s",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"],
+                       "build_L": wp["build_L"], "rabitq_bits": 4, "k": k, "beam_width": L,
+                       "queries_per_step_per_gpu": B, "parallelism": f"replicas x{dist.world}",
+                       "l2": "index 0.58 GB larger than L2, not flushed; fresh query batch every step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": tr, "peak_source": f"{peak_kind} hbm_gbs",
+                         "kernel": "search_kernel", "kernel_ms": search_avg_ms,
+                         "bytes_per_query": bq, "per_query": {"H": H, "E": E, "C_r": Cr}},
+            "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": B * wp["dim"] * 4,
+                    "d2h_bytes_per_step": B * k * 8},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+            "recall_at_10": rec,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.close()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -66,6 +66,10 @@ struct Device {
   uint32_t* work = nullptr;
   uint32_t* ovf = nullptr;
   size_t ovf_slots = 0;
+  // kernel timing ring: (before prepare, after prepare, after search)
+  static constexpr size_t kRing = 4096;
+  std::vector<cudaEvent_t> tev;
+  size_t tcount = 0;
 
   void release() {
     if (ordinal < 0) return;
@@ -86,6 +90,8 @@ struct Device {
     dev_free(ovf);
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
+    for (cudaEvent_t e : tev) cudaEventDestroy(e);
+    tev.clear();
     if (stream) cudaStreamDestroy(stream);
     ev0 = ev1 = nullptr;
     stream = nullptr;
@@ -218,6 +224,7 @@ struct dvs_index {
   std::vector<dvs::Device> devs;
   uint32_t hop_limit = 0;
   uint32_t slots_per_entry = dvs::kDefaultSlotsPerBeamEntry;
+  bool kernel_timing = false;
   std::mutex mu;
 };
 
@@ -249,11 +256,21 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
     d.ovf_slots = slots;
   }
   DVS_CUDA(cudaMemsetAsync(d.work, 0, 16, st));
+  cudaEvent_t* tr = nullptr;
+  if (ix->kernel_timing) {
+    if (d.tev.empty()) {
+      d.tev.resize(3 * Device::kRing);
+      for (auto& e : d.tev) DVS_CUDA(cudaEventCreate(&e));
+    }
+    if (d.tcount < Device::kRing) tr = &d.tev[3 * d.tcount++];
+  }
   if (timed) DVS_CUDA(cudaEventRecord(d.ev0, st));
+  if (tr) DVS_CUDA(cudaEventRecord(tr[0], st));
   if (rabitq) {
     DVS_CUDA(launch_prepare(d_q, lay.dim, lay.P, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits, nq,
                             st));
   }
+  if (tr) DVS_CUDA(cudaEventRecord(tr[1], st));
   SearchArgs a;
   a.ix = lay;
   a.queries = d_q;
@@ -277,6 +294,7 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
   a.cap_pad = s.cap_pad;
   a.dim_pad = lay.vec_stride;
   DVS_CUDA(launch_search(a, s.wpb, blocks, st));
+  if (tr) DVS_CUDA(cudaEventRecord(tr[2], st));
   if (timed) DVS_CUDA(cudaEventRecord(d.ev1, st));
   return DVS_OK;
 }
@@ -382,6 +400,35 @@ dvs_status dvs_set_visited_slots(dvs_index* ix, uint32_t slots_per_beam_entry) {
     return fail(DVS_ERR_ARG, "visited slots per beam entry must be in 2..256");
   std::lock_guard<std::mutex> g(ix->mu);
   ix->slots_per_entry = slots_per_beam_entry;
+  return DVS_OK;
+}
+
+dvs_status dvs_set_kernel_timing(dvs_index* ix, int enable) {
+  if (!ix) return fail(DVS_ERR_ARG, "null index");
+  std::lock_guard<std::mutex> g(ix->mu);
+  ix->kernel_timing = enable != 0;
+  return DVS_OK;
+}
+
+dvs_status dvs_kernel_times(dvs_index* ix, uint32_t slot, uint32_t* searches, double* prepare_ms, double* search_ms) {
+  if (!ix || !searches || !prepare_ms || !search_ms) return fail(DVS_ERR_ARG, "null argument");
+  if (slot >= ix->devs.size()) return fail(DVS_ERR_ARG, "device slot out of range");
+  std::lock_guard<std::mutex> g(ix->mu);
+  dvs::Device& d = ix->devs[slot];
+  DVS_CUDA(cudaSetDevice(d.ordinal));
+  double pm = 0.0, sm = 0.0;
+  for (size_t i = 0; i < d.tcount; ++i) {
+    DVS_CUDA(cudaEventSynchronize(d.tev[3 * i + 2]));
+    float a = 0.f, b = 0.f;
+    DVS_CUDA(cudaEventElapsedTime(&a, d.tev[3 * i], d.tev[3 * i + 1]));
+    DVS_CUDA(cudaEventElapsedTime(&b, d.tev[3 * i + 1], d.tev[3 * i + 2]));
+    pm += a;
+    sm += b;
+  }
+  *searches = uint32_t(d.tcount);
+  *prepare_ms = pm;
+  *search_ms = sm;
+  d.tcount = 0;
   return DVS_OK;
 }
 

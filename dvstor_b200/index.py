@@ -60,6 +60,15 @@ class Index:
     def set_hop_limit(self, max_expansions: int) -> None:
         check(lib().dvs_set_hop_limit(self._h, max_expansions))
 
+    def set_kernel_timing(self, enable: bool) -> None:
+        check(lib().dvs_set_kernel_timing(self._h, 1 if enable else 0))
+
+    def kernel_times(self, device_slot: int = 0):
+        """(searches, prepare_ms_sum, search_ms_sum) recorded since the last call."""
+        n, pm, sm = C.c_uint32(), C.c_double(), C.c_double()
+        check(lib().dvs_kernel_times(self._h, device_slot, C.byref(n), C.byref(pm), C.byref(sm)))
+        return n.value, pm.value, sm.value
+
     def set_visited_slots(self, slots_per_beam_entry: int) -> None:
         check(lib().dvs_set_visited_slots(self._h, slots_per_beam_entry))
 

