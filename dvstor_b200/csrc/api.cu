@@ -39,7 +39,7 @@ void dev_free(T*& p) {
 
 // Visited-set sizing: default shared-memory slots per beam entry and the spill table.
 constexpr uint32_t kDefaultSlotsPerBeamEntry = 48;
-constexpr uint32_t kOverflowSlots = 1u << 16;
+constexpr uint32_t kOverflowSlots = 1u << 14;
 
 struct Device {
   int ordinal = 0;
@@ -199,7 +199,7 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, Launc
     const size_t smem = size_t(wpb) * words * 4;
     if (smem > 227 * 1024) break;
     int bps = 0;
-    const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, wpb, smem, &bps);
+    const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, wpb, smem, &bps);
     if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
     if (int(wpb) * bps > best_warps) {
       best_warps = int(wpb) * bps;
@@ -211,7 +211,7 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, Launc
     return fail(DVS_ERR_CAPACITY, "beam capacity " + std::to_string(cap) + " needs more shared memory than a block has");
   // set the attribute for the chosen configuration last
   int bps = 0;
-  const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, s.wpb, size_t(s.wpb) * words * 4, &bps);
+  const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, s.wpb, size_t(s.wpb) * words * 4, &bps);
   if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
   return DVS_OK;
 }
@@ -290,7 +290,7 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
   a.ovf_cap = kOverflowSlots;
   a.ovf_limit = kOverflowSlots / 10 * 8;
   a.hcap = s.hcap;
-  a.hlimit = s.hcap / 10 * 8;
+  a.hlimit = s.hcap / 10 * 9;
   a.cap_pad = s.cap_pad;
   a.dim_pad = lay.vec_stride;
   DVS_CUDA(launch_search(a, s.wpb, blocks, st));

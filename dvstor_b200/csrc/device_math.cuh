@@ -104,7 +104,19 @@ __device__ __forceinline__ void rabitq_word(uint32_t word, const float* __restri
                                             float& s0, float& s1, float& s2, float& s3) {
   constexpr int kPer = 32 / BITS;
   constexpr uint32_t kMask = (1u << BITS) - 1u;
-  if (j0 + kPer <= dim) {
+  if (BITS == 4 && j0 + kPer <= dim) {
+    // nibble n of the word sits in byte n/2 of (n even ? lo : hi); PRMT places
+    // it under the exponent of 2^23 so a subtraction yields the exact value
+    const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int b = 0; b < 4; b += 2) {
+      const float4 qv = *reinterpret_cast<const float4*>(qr + j0 + 2 * b);
+      s0 = __fmaf_rn(__fsub_rn(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u + b)), 8388608.0f), qv.x, s0);
+      s1 = __fmaf_rn(__fsub_rn(__uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u + b)), 8388608.0f), qv.y, s1);
+      s2 = __fmaf_rn(__fsub_rn(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7441u + b)), 8388608.0f), qv.z, s2);
+      s3 = __fmaf_rn(__fsub_rn(__uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7441u + b)), 8388608.0f), qv.w, s3);
+    }
+  } else if (j0 + kPer <= dim) {
 #pragma unroll
     for (int n = 0; n < kPer; n += 4) {
       const float4 qv = *reinterpret_cast<const float4*>(qr + j0 + n);

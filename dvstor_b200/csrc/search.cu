@@ -52,14 +52,44 @@ __device__ __forceinline__ bool table_insert(uint32_t* tab, uint32_t cap, uint32
   return false;
 }
 
-__device__ __forceinline__ bool table_contains(const uint32_t* tab, uint32_t cap, uint32_t id) {
-  const volatile uint32_t* vt = tab;
-  uint32_t s = hash_slot(id, cap);
-  for (uint32_t probe = 0; probe < cap; ++probe) {
-    const uint32_t cur = vt[s];
-    if (cur == id) return true;
-    if (cur == kEmptySlot) return false;
-    s = (s + 1 == cap) ? 0 : s + 1;
+// Shared-memory visited table probed in buckets of four slots (one 16-byte
+// load per step): an id lives in the first bucket of its probe sequence that
+// had a free slot when it was inserted, and slots never empty during a query,
+// so a bucket with a free slot that lacks the id ends the search.
+__device__ __forceinline__ uint4 load_bucket(const uint32_t* tab, uint32_t b) {
+  uint4 v;
+  asm volatile("ld.volatile.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(tab + 4 * b))));
+  return v;
+}
+
+__device__ __forceinline__ bool bucket_insert(uint32_t* tab, uint32_t nbuckets, uint32_t id) {
+  uint32_t b = hash_slot(id, nbuckets);
+  for (uint32_t probe = 0; probe < nbuckets; ++probe) {
+    const uint4 v = load_bucket(tab, b);
+    if (v.x == id || v.y == id || v.z == id || v.w == id) return false;
+    const uint32_t sl[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (sl[e] == kEmptySlot) {
+        const uint32_t old = atomicCAS(tab + 4 * b + e, kEmptySlot, id);
+        if (old == kEmptySlot) return true;
+        if (old == id) return false;
+      }
+    }
+    b = (b + 1 == nbuckets) ? 0 : b + 1;
+  }
+  return false;
+}
+
+__device__ __forceinline__ bool bucket_contains(const uint32_t* tab, uint32_t nbuckets, uint32_t id) {
+  uint32_t b = hash_slot(id, nbuckets);
+  for (uint32_t probe = 0; probe < nbuckets; ++probe) {
+    const uint4 v = load_bucket(tab, b);
+    if (v.x == id || v.y == id || v.z == id || v.w == id) return true;
+    if (v.x == kEmptySlot || v.y == kEmptySlot || v.z == kEmptySlot || v.w == kEmptySlot) return false;
+    b = (b + 1 == nbuckets) ? 0 : b + 1;
   }
   return false;
 }
@@ -115,8 +145,47 @@ __device__ __forceinline__ void l2_rows_warp(const DevLayout& ix, const float* _
   }
 }
 
-template <int BITS, int NPL>
-__global__ void __launch_bounds__(256) search_kernel(const SearchArgs a) {
+// RaBitQ estimate of a record already held in registers (RCH 16-byte chunks).
+template <int BITS, int RCH>
+__device__ __forceinline__ float estimate_regs(const uint4 (&v)[RCH], const DevLayout& ix, const float* __restrict__ qr,
+                                               float q_add, float q_k1) {
+  constexpr int kPer = 32 / BITS;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, add_o = 0.f, rs_o = 0.f;
+#pragma unroll
+  for (int t = 0; t < RCH; ++t) {
+    const uint32_t w[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t wi = t * 4 + e;
+      if (wi < ix.code_words)
+        rabitq_word<BITS>(w[e], qr, wi * kPer, ix.dim, s0, s1, s2, s3);
+      else if (wi == ix.code_words)
+        add_o = __uint_as_float(w[e]);
+      else if (wi == ix.code_words + 1)
+        rs_o = __uint_as_float(w[e]);
+    }
+  }
+  return rabitq_finish(tile4_sum(s0, s1, s2, s3), add_o, rs_o, q_add, q_k1, float((1u << BITS) - 1u));
+}
+
+// Warp-uniform first index p >= lo of a sorted shared array with a[p] >= x.
+__device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n, float x) {
+  uint32_t lo = 0, hi = n;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (a[mid] < x)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+// BITS: code width.  NPL: adjacency slots per lane (R <= 32 * NPL).  RCH: 16-byte
+// chunks of a RaBitQ record a lane holds in registers (0 = records too large:
+// they are loaded after the visited check instead).
+template <int BITS, int NPL, int RCH>
+__global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint32_t smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const DevLayout& ix = a.ix;
@@ -129,11 +198,17 @@ __global__ void __launch_bounds__(256) search_kernel(const SearchArgs a) {
   float* qr = qv + a.dim_pad;
   uint32_t* cid = base + 4 * a.cap_pad + 2 * a.dim_pad;
   float* cd = reinterpret_cast<float*>(cid + 64);
-  uint32_t* htab = cid + 128;
+  float* sd = reinterpret_cast<float*>(cid + 128);
+  uint32_t* sid = cid + 192;
+  uint32_t* htab = cid + 256;
   const uint32_t warp_slot = blockIdx.x * (blockDim.x >> 5) + wib;
   uint32_t* gtab = a.ovf ? a.ovf + size_t(warp_slot) * a.ovf_cap : nullptr;
   const bool rabitq = a.mode == 0;
   const uint32_t dim = ix.dim, R = ix.R;
+  const uint32_t rec_stride4 = ix.rec_words >> 2;
+  const uint32_t nch = (ix.code_words + 2 + 3) >> 2;
+  const uint4* rec4 = reinterpret_cast<const uint4*>(ix.rec);
+  const float kInf = __int_as_float(0x7F800000);
 
   for (;;) {
     uint32_t qi = 0;
@@ -161,25 +236,30 @@ __global__ void __launch_bounds__(256) search_kernel(const SearchArgs a) {
     if (lane == 0) {
       bdA[0] = md;
       biA[0] = ix.medoid;
-      htab[hash_slot(ix.medoid, a.hcap)] = ix.medoid;
+      htab[4 * hash_slot(ix.medoid, a.hcap >> 2)] = ix.medoid;
     }
     __syncwarp();
     float* bd = bdA;
     uint32_t* bi = biA;
     float* bdo = bdB;
     uint32_t* bio = biB;
-    uint32_t nb = 1, hcount = 1, gcount = 0, H = 0, E = 0, err = 0;
+    uint32_t nb = 1, hcount = 1, gcount = 0, H = 0, E = 0, err = 0, scan_from = 0;
     bool overflow = false;
+    uint32_t pf_node = kEmptySlot, pf[NPL];
 
     for (;;) {
       // ---- select the first unexpanded entry (vamana.hh:134-141) ----
-      int best = -1;
-      for (uint32_t b = 0; b < nb; b += 32) {
+      // entries before scan_from are expanded or not selectable; the next
+      // selectable entry of the same chunk is the guess for the following hop
+      int best = -1, next = -1;
+      for (uint32_t b = scan_from & ~31u; b < nb; b += 32) {
         const uint32_t p = b + lane;
         const bool ok = p < nb && !(bi[p] & kExpandedBit) && bd[p] < FLT_MAX;
-        const uint32_t m = __ballot_sync(kFull, ok);
-        if (m) {
-          best = int(b + __ffs(m) - 1);
+        const uint32_t msk = __ballot_sync(kFull, ok);
+        if (msk) {
+          best = int(b + __ffs(msk) - 1);
+          const uint32_t rest = msk & (msk - 1);
+          if (rest) next = int(b + __ffs(rest) - 1);
           break;
         }
       }
@@ -189,20 +269,45 @@ __global__ void __launch_bounds__(256) search_kernel(const SearchArgs a) {
         break;
       }
       const uint32_t u = bi[best];
+      const uint32_t guess = next >= 0 ? bi[next] : kEmptySlot;
       __syncwarp();
       if (lane == 0) bi[best] = u | kExpandedBit;
       ++H;
 
-      // ---- neighbours, visited filter (vamana.hh:162-182) ----
+      // ---- neighbours (vamana.hh:162-168): prefetched one hop ahead when guessed ----
       uint32_t nbr[NPL];
+      const bool hit = u == pf_node;
 #pragma unroll
       for (int s = 0; s < NPL; ++s) {
         const uint32_t j = lane + 32u * s;
-        nbr[s] = j < R ? __ldg(ix.adj + size_t(u) * R + j) : kEmptySlot;
+        nbr[s] = hit ? pf[s] : (j < R ? __ldg(ix.adj + size_t(u) * R + j) : kEmptySlot);
       }
-      uint32_t m = 0;
+      pf_node = guess;
 #pragma unroll
       for (int s = 0; s < NPL; ++s) {
+        const uint32_t j = lane + 32u * s;
+        pf[s] = (guess != kEmptySlot && j < R) ? __ldg(ix.adj + size_t(guess) * R + j) : kEmptySlot;
+      }
+      // records of every listed neighbour are requested before the visited
+      // check so their latency overlaps it; visited ones are discarded
+      uint4 rv[NPL][RCH > 0 ? RCH : 1];
+      if (RCH > 0 && rabitq) {
+#pragma unroll
+        for (int s = 0; s < NPL; ++s) {
+          if (nbr[s] != kEmptySlot) {
+#pragma unroll
+            for (int c = 0; c < RCH; ++c)
+              if (c < int(nch)) rv[s][c] = __ldg(rec4 + size_t(nbr[s]) * rec_stride4 + c);
+          }
+        }
+      }
+
+      // ---- visited filter (vamana.hh:172-182) ----
+      uint32_t m = 0;
+      bool fresh[NPL];
+#pragma unroll
+      for (int s = 0; s < NPL; ++s) {
+        fresh[s] = false;
         const uint32_t peers = __match_any_sync(kFull, nbr[s]);
         const bool first = nbr[s] != kEmptySlot && (peers & lanemask_lt()) == 0;
         if (!overflow && hcount + 32 > a.hlimit) {
@@ -218,69 +323,116 @@ __global__ void __launch_bounds__(256) search_kernel(const SearchArgs a) {
         }
         if (overflow && gcount + 32 > a.ovf_limit) err |= kErrCapacity;
         if (err & kErrCapacity) break;
-        bool fresh = false;
         if (first) {
           if (!overflow)
-            fresh = table_insert(htab, a.hcap, nbr[s]);
+            fresh[s] = bucket_insert(htab, a.hcap >> 2, nbr[s]);
           else
-            fresh = !table_contains(htab, a.hcap, nbr[s]) && table_insert(gtab, a.ovf_cap, nbr[s]);
+            fresh[s] = !bucket_contains(htab, a.hcap >> 2, nbr[s]) && table_insert(gtab, a.ovf_cap, nbr[s]);
         }
-        const uint32_t bal = __ballot_sync(kFull, fresh);
-        if (fresh) cid[m + __popc(bal & lanemask_lt())] = nbr[s];
-        const uint32_t cnt = __popc(bal);
+        const uint32_t cnt = __popc(__ballot_sync(kFull, fresh[s]));
         m += cnt;
         if (overflow)
           gcount += cnt;
         else
           hcount += cnt;
-        __syncwarp();
       }
       if (err & kErrCapacity) break;
-      if (m == 0) continue;
+      if (m == 0) {
+        scan_from = best + 1;
+        continue;
+      }
       E += m;
 
-      // ---- distances of the unvisited neighbours ----
-      if (rabitq) {
-        for (uint32_t i = lane; i < m; i += 32) cd[i] = estimate_lane<BITS>(ix, cid[i], qr, q_add, q_k1);
-      } else {
+      // ---- distances of the unvisited neighbours, staged in insertion order ----
+      {
+        uint32_t base_pos = 0;
+#pragma unroll
+        for (int s = 0; s < NPL; ++s) {
+          const uint32_t bal = __ballot_sync(kFull, fresh[s]);
+          if (fresh[s]) {
+            const uint32_t pos = base_pos + __popc(bal & lanemask_lt());
+            cid[pos] = nbr[s];
+            if (RCH > 0 && rabitq) cd[pos] = estimate_regs<BITS, (RCH > 0 ? RCH : 1)>(rv[s], ix, qr, q_add, q_k1);
+          }
+          base_pos += __popc(bal);
+        }
+      }
+      __syncwarp();
+      if (!rabitq) {
         l2_rows_warp(ix, qv, cid, m, cd, lane, 0xFFFFFFFFu);
+      } else if (RCH == 0) {
+        for (uint32_t i = lane; i < m; i += 32) cd[i] = estimate_lane<BITS>(ix, cid[i], qr, q_add, q_k1);
       }
       __syncwarp();
 
       // ---- insert_into_beam for all m candidates (vamana.hh:347-352, 1014-1030) ----
-      const uint32_t nb_new = min(a.cap, nb + m);
-      for (uint32_t i = lane; i < m; i += 32) {
-        const float d = cd[i];
-        uint32_t r = 0;
-        for (uint32_t j = 0; j < m; ++j) {
-          const float dj = cd[j];
-          r += (dj < d) || (dj == d && j > i);
+      // A full beam drops every candidate farther than its last entry; those can
+      // neither survive nor move a survivor, so they leave the merge first.  The
+      // survivors are ranked by (distance, later insertion first); survivor i
+      // lands at rank_i + ins_i (ins_i = beam entries strictly closer) and beam
+      // entry p moves down by #{i : ins_i <= p} (candidates not farther than it).
+      const float worst = nb == a.cap ? bd[a.cap - 1] : kInf;
+      uint32_t ms = 0;
+#pragma unroll
+      for (int h = 0; h < NPL; ++h) {
+        const uint32_t i = 32u * h + lane;
+        const float d = i < m ? cd[i] : 0.f;
+        const bool keep = i < m && d <= worst;
+        const uint32_t bal = __ballot_sync(kFull, keep);
+        if (keep) {
+          sd[ms + __popc(bal & lanemask_lt())] = d;
+          sid[ms + __popc(bal & lanemask_lt())] = cid[i];
         }
-        if (r >= a.cap) continue;
-        uint32_t lo = 0, hi = nb;
-        while (lo < hi) {
-          const uint32_t mid = (lo + hi) >> 1;
-          if (bd[mid] < d)
-            lo = mid + 1;
-          else
-            hi = mid;
-        }
-        const uint32_t pos = r + lo;
-        if (pos < a.cap) {
-          bdo[pos] = d;
-          bio[pos] = cid[i];
+        ms += __popc(bal);
+      }
+      if (ms == 0) {
+        scan_from = best + 1;
+        continue;
+      }
+      __syncwarp();
+      float nd[NPL];
+      uint32_t nid[NPL], rank[NPL], ins[NPL];
+#pragma unroll
+      for (int h = 0; h < NPL; ++h) {
+        const uint32_t i = 32u * h + lane;
+        nd[h] = i < ms ? sd[i] : kInf;
+        nid[h] = i < ms ? sid[i] : 0u;
+        rank[h] = 0;
+        ins[h] = i < ms ? lower_bound_smem(bd, nb, nd[h]) : 0xFFFFFFFFu;
+      }
+      for (uint32_t j = 0; j < ms; ++j) {
+        const float dj = __shfl_sync(kFull, nd[j >> 5], j & 31);
+#pragma unroll
+        for (int h = 0; h < NPL; ++h) {
+          const uint32_t i = 32u * h + lane;
+          rank[h] += (dj < nd[h]) || (dj == nd[h] && j > i);
         }
       }
-      for (uint32_t p = lane; p < nb; p += 32) {
-        const float d = bd[p];
-        uint32_t c = 0;
-        for (uint32_t j = 0; j < m; ++j) c += cd[j] <= d;
-        const uint32_t pos = p + c;
-        if (pos < a.cap) {
-          bdo[pos] = d;
-          bio[pos] = bi[p];
+      uint32_t first_pos = 0xFFFFFFFFu;
+#pragma unroll
+      for (int h = 0; h < NPL; ++h) {
+        const uint32_t i = 32u * h + lane;
+        if (i < ms) {
+          const uint32_t pos = rank[h] + ins[h];
+          first_pos = min(first_pos, pos);
+          if (pos < a.cap) {
+            bdo[pos] = nd[h];
+            bio[pos] = nid[h];
+          }
         }
       }
+      first_pos = __reduce_min_sync(kFull, first_pos);
+      for (uint32_t p0 = 0; p0 < nb; p0 += 32) {
+        const uint32_t p = p0 + lane;
+        uint32_t shift = 0;
+        for (uint32_t j = 0; j < ms; ++j) shift += __shfl_sync(kFull, ins[j >> 5], j & 31) <= p;
+        if (p < nb && p + shift < a.cap) {
+          bdo[p + shift] = bd[p];
+          bio[p + shift] = bi[p];
+        }
+      }
+      scan_from = min(first_pos, uint32_t(best) + 1);
+      const uint32_t nb_new = min(a.cap, nb + ms);
       __syncwarp();
       float* tf = bd;
       bd = bdo;
@@ -318,7 +470,7 @@ __global__ void __launch_bounds__(256) search_kernel(const SearchArgs a) {
     }
     for (uint32_t r = nb + lane; r < a.k; r += 32) {
       a.out_ids[size_t(qi) * a.k + r] = kEmptySlot;
-      a.out_dist[size_t(qi) * a.k + r] = __int_as_float(0x7F800000);
+      a.out_dist[size_t(qi) * a.k + r] = kInf;
     }
     if (lane == 0) {
       if (a.counters) {
@@ -432,16 +584,40 @@ __global__ void l2_rows_kernel(const float* __restrict__ q, const float* __restr
   if (row < n && t == 0) out[row] = acc;
 }
 
-template <int BITS, int NPL>
-cudaError_t set_attr(size_t smem) {
-  return cudaFuncSetAttribute(search_kernel<BITS, NPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+template <int BITS, int NPL, int RCH>
+cudaError_t occ(uint32_t wpb, size_t smem, int* bps) {
+  cudaError_t e = cudaFuncSetAttribute(search_kernel<BITS, NPL, RCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(smem));
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(bps, search_kernel<BITS, NPL, RCH>, int(wpb * 32), smem);
+}
+
+template <int BITS, int NPL, int RCH>
+void launch(const SearchArgs& a, dim3 grid, dim3 block, size_t smem, cudaStream_t st) {
+  search_kernel<BITS, NPL, RCH><<<grid, block, smem, st>>>(a);
+}
+
+// Record chunks a lane keeps in registers: 4 (<= 64-byte records) or 8
+// (<= 128 bytes); larger records are loaded after the visited check.
+inline int record_chunks(uint32_t code_words) {
+  const uint32_t nch = (code_words + 2 + 3) / 4;
+  return nch <= 4 ? 4 : nch <= 8 ? 8 : 0;
 }
 
 template <int BITS, int NPL>
-cudaError_t occ(uint32_t wpb, size_t smem, int* bps) {
-  cudaError_t e = set_attr<BITS, NPL>(smem);
-  if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(bps, search_kernel<BITS, NPL>, int(wpb * 32), smem);
+cudaError_t occ_rch(int rch, uint32_t wpb, size_t smem, int* bps) {
+  return rch == 4 ? occ<BITS, NPL, 4>(wpb, smem, bps) : rch == 8 ? occ<BITS, NPL, 8>(wpb, smem, bps)
+                                                            : occ<BITS, NPL, 0>(wpb, smem, bps);
+}
+
+template <int BITS, int NPL>
+void launch_rch(int rch, const SearchArgs& a, dim3 g, dim3 b, size_t smem, cudaStream_t st) {
+  if (rch == 4)
+    launch<BITS, NPL, 4>(a, g, b, smem, st);
+  else if (rch == 8)
+    launch<BITS, NPL, 8>(a, g, b, smem, st);
+  else
+    launch<BITS, NPL, 0>(a, g, b, smem, st);
 }
 
 }  // namespace
@@ -457,12 +633,13 @@ cudaError_t launch_prepare(const float* queries, uint32_t q_stride, const float*
   return cudaGetLastError();
 }
 
-cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t wpb, size_t smem, int* bps) {
+cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, uint32_t wpb, size_t smem, int* bps) {
   const bool two = R > 32;
+  const int rch = record_chunks(code_words);
   switch (bits) {
-    case 1: return two ? occ<1, 2>(wpb, smem, bps) : occ<1, 1>(wpb, smem, bps);
-    case 2: return two ? occ<2, 2>(wpb, smem, bps) : occ<2, 1>(wpb, smem, bps);
-    case 4: return two ? occ<4, 2>(wpb, smem, bps) : occ<4, 1>(wpb, smem, bps);
+    case 1: return two ? occ_rch<1, 2>(rch, wpb, smem, bps) : occ_rch<1, 1>(rch, wpb, smem, bps);
+    case 2: return two ? occ_rch<2, 2>(rch, wpb, smem, bps) : occ_rch<2, 1>(rch, wpb, smem, bps);
+    case 4: return two ? occ_rch<4, 2>(rch, wpb, smem, bps) : occ_rch<4, 1>(rch, wpb, smem, bps);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -470,19 +647,17 @@ cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t wpb, size_t sme
 cudaError_t launch_search(const SearchArgs& a, uint32_t wpb, uint32_t blocks, cudaStream_t stream) {
   const size_t smem = size_t(wpb) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap) * 4;
   const bool two = a.ix.R > 32;
+  const int rch = record_chunks(a.ix.code_words);
   const dim3 grid(blocks), block(wpb * 32);
   switch (a.ix.bits) {
     case 1:
-      if (two) search_kernel<1, 2><<<grid, block, smem, stream>>>(a);
-      else search_kernel<1, 1><<<grid, block, smem, stream>>>(a);
+      two ? launch_rch<1, 2>(rch, a, grid, block, smem, stream) : launch_rch<1, 1>(rch, a, grid, block, smem, stream);
       break;
     case 2:
-      if (two) search_kernel<2, 2><<<grid, block, smem, stream>>>(a);
-      else search_kernel<2, 1><<<grid, block, smem, stream>>>(a);
+      two ? launch_rch<2, 2>(rch, a, grid, block, smem, stream) : launch_rch<2, 1>(rch, a, grid, block, smem, stream);
       break;
     case 4:
-      if (two) search_kernel<4, 2><<<grid, block, smem, stream>>>(a);
-      else search_kernel<4, 1><<<grid, block, smem, stream>>>(a);
+      two ? launch_rch<4, 2>(rch, a, grid, block, smem, stream) : launch_rch<4, 1>(rch, a, grid, block, smem, stream);
       break;
     default:
       return cudaErrorInvalidValue;

@@ -46,7 +46,7 @@ constexpr uint32_t kErrHopLimit = 2u;
 
 // Words of shared memory one warp of the search kernel uses.
 __host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap) {
-  return 4 * cap_pad + 2 * dim_pad + 128 + hcap;
+  return 4 * cap_pad + 2 * dim_pad + 256 + hcap;
 }
 
 cudaError_t launch_prepare(const float* queries, uint32_t q_stride, const float* P, const float* c_rot, float* qrot,
@@ -59,7 +59,8 @@ cudaError_t launch_search(const SearchArgs& a, uint32_t warps_per_block, uint32_
 
 // Occupancy helper: blocks per SM for `warps_per_block` warps with the given
 // per-warp shared memory; also sets the kernel's dynamic smem attribute.
-cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t warps_per_block, size_t smem_bytes, int* blocks_per_sm);
+cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, uint32_t warps_per_block, size_t smem_bytes,
+                             int* blocks_per_sm);
 
 cudaError_t launch_estimate_ref_layout(const float* qrot, const float* f3, const uint8_t* records, float* out,
                                        uint32_t n, uint32_t dim, uint32_t bits, cudaStream_t stream);

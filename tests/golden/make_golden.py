@@ -32,8 +32,13 @@ def main(out_dir):
     lib.ref_query_prepare.argtypes = [vp, vp, vp, vp, vp, u32, u32]
     lib.ref_quantize_single.argtypes = [vp, vp, vp, vp, u32, u32, C.c_double]
 
+    keep = []  # device buffers stay alive until the reference kernels have run
+
     def dev(a):
-        return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        keep.append(t)
+        torch.cuda.synchronize()
+        return t
 
     def p(t):
         return C.c_void_p(t.data_ptr())
