@@ -37,8 +37,10 @@ void dev_free(T*& p) {
   p = nullptr;
 }
 
-// Visited-set sizing: default shared-memory slots per beam entry and the spill table.
-constexpr uint32_t kDefaultSlotsPerBeamEntry = 48;
+// Visited-set sizing: default shared-memory slots per beam entry (32-bit table
+// for indexes of 2^24 nodes or more, compact 16-bit table below) and the spill table.
+constexpr uint32_t kDefaultSlots32 = 48;
+constexpr uint32_t kDefaultSlots16 = 48;
 constexpr uint32_t kOverflowSlots = 1u << 14;
 
 struct Device {
@@ -100,6 +102,7 @@ struct Device {
 
 struct LaunchShape {
   uint32_t cap = 0, cap_pad = 0, hcap = 0, wpb = 0, blocks_per_sm = 0;
+  uint32_t vt16 = 0, hbuckets = 0, hlimit = 0;
 };
 
 dvs_status upload(Device& d, const HostIndex& h) {
@@ -192,7 +195,19 @@ dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path) {
 dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, LaunchShape& s) {
   s.cap = cap;
   s.cap_pad = (cap + 31) / 32 * 32;
-  s.hcap = std::max(64u, (cap * slots_per_entry + 31) / 32 * 32);
+  if (d.lay.n < (1u << 24)) {
+    // 16-bit entries, 8 per 16-byte bucket; at least 1024 buckets.  The entry
+    // limit follows slots_per_entry even where the bucket minimum is larger.
+    const uint32_t spe = slots_per_entry ? slots_per_entry : kDefaultSlots16;
+    s.vt16 = 1;
+    s.hbuckets = std::max(1024u, (cap * spe + 7) / 8);
+    s.hcap = s.hbuckets * 4;
+    s.hlimit = std::min(s.hbuckets * 8, cap * spe) / 10 * 9;
+  } else {
+    const uint32_t spe = slots_per_entry ? slots_per_entry : kDefaultSlots32;
+    s.hcap = std::max(64u, (cap * spe + 31) / 32 * 32);
+    s.hlimit = s.hcap / 10 * 9;
+  }
   const uint32_t words = search_warp_words(s.cap_pad, d.lay.vec_stride, s.hcap);
   int best_warps = 0;
   for (uint32_t wpb : {1u, 2u, 4u, 8u}) {
@@ -223,7 +238,7 @@ struct dvs_index {
   dvs::HostIndex host;              // kept for downloads and metadata
   std::vector<dvs::Device> devs;
   uint32_t hop_limit = 0;
-  uint32_t slots_per_entry = dvs::kDefaultSlotsPerBeamEntry;
+  uint32_t slots_per_entry = 0;  // 0 = the default of the table kind in use
   bool kernel_timing = false;
   std::mutex mu;
 };
@@ -290,7 +305,10 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
   a.ovf_cap = kOverflowSlots;
   a.ovf_limit = kOverflowSlots / 10 * 8;
   a.hcap = s.hcap;
-  a.hlimit = s.hcap / 10 * 9;
+  a.hlimit = s.hlimit;
+  a.vt16 = s.vt16;
+  a.hbuckets = s.hbuckets;
+  a.inv_hbuckets = s.hbuckets ? 1.0f / float(s.hbuckets) : 0.f;
   a.cap_pad = s.cap_pad;
   a.dim_pad = lay.vec_stride;
   DVS_CUDA(launch_search(a, s.wpb, blocks, st));
@@ -396,7 +414,7 @@ dvs_status dvs_set_hop_limit(dvs_index* ix, uint32_t max_expansions) {
 
 dvs_status dvs_set_visited_slots(dvs_index* ix, uint32_t slots_per_beam_entry) {
   if (!ix) return fail(DVS_ERR_ARG, "null index");
-  if (slots_per_beam_entry < 2 || slots_per_beam_entry > 256)
+  if (slots_per_beam_entry != 0 && (slots_per_beam_entry < 2 || slots_per_beam_entry > 256))
     return fail(DVS_ERR_ARG, "visited slots per beam entry must be in 2..256");
   std::lock_guard<std::mutex> g(ix->mu);
   ix->slots_per_entry = slots_per_beam_entry;

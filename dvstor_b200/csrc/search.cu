@@ -52,6 +52,18 @@ __device__ __forceinline__ bool table_insert(uint32_t* tab, uint32_t cap, uint32
   return false;
 }
 
+__device__ __forceinline__ bool table_contains(const uint32_t* tab, uint32_t cap, uint32_t id) {
+  const volatile uint32_t* vt = tab;
+  uint32_t s = hash_slot(id, cap);
+  for (uint32_t probe = 0; probe < cap; ++probe) {
+    const uint32_t cur = vt[s];
+    if (cur == id) return true;
+    if (cur == kEmptySlot) return false;
+    s = (s + 1 == cap) ? 0 : s + 1;
+  }
+  return false;
+}
+
 // Shared-memory visited table probed in buckets of four slots (one 16-byte
 // load per step): an id lives in the first bucket of its probe sequence that
 // had a free slot when it was inserted, and slots never empty during a query,
@@ -92,6 +104,81 @@ __device__ __forceinline__ bool bucket_contains(const uint32_t* tab, uint32_t nb
     b = (b + 1 == nbuckets) ? 0 : b + 1;
   }
   return false;
+}
+
+// Compact visited table for indexes of fewer than 2^24 nodes: NB buckets of
+// eight 16-bit entries, two-choice placement.  An id is mixed by two 24-bit
+// bijections h1, h2; for hash k it may live in bucket hk mod NB as the entry
+// (k << 14) | (hk div NB).  (bucket, entry) determines hk and hence the id, so
+// membership is exact with half the bytes of a 32-bit table, and a lookup is
+// two independent 16-byte loads instead of a probe chain.  0xFFFF is empty
+// (entries use 15 bits; NB >= 1024 keeps hk div NB below 2^14).
+__device__ __forceinline__ uint32_t mix24(uint32_t x) {
+  x = (x * 0x9E3779u) & 0xFFFFFFu;
+  x ^= x >> 12;
+  x = (x * 0x85EBCBu) & 0xFFFFFFu;
+  x ^= x >> 11;
+  return x;
+}
+
+struct Slot16 {
+  uint32_t b, tag;
+};
+
+__device__ __forceinline__ Slot16 split16(uint32_t h, uint32_t nb, float inv_nb, uint32_t which) {
+  uint32_t q = __float2uint_rz(__fmul_rz(float(h), inv_nb));
+  int32_t r = int32_t(h) - int32_t(q * nb);
+  if (r < 0) {
+    --q;
+    r += int32_t(nb);
+  } else if (r >= int32_t(nb)) {
+    ++q;
+    r -= int32_t(nb);
+  }
+  return {uint32_t(r), (which << 14) | q};
+}
+
+__device__ __forceinline__ bool holds16(const uint4& v, uint32_t tag) {
+  const uint32_t t = tag * 0x10001u;
+  return (__vcmpeq2(v.x, t) | __vcmpeq2(v.y, t) | __vcmpeq2(v.z, t) | __vcmpeq2(v.w, t)) != 0;
+}
+
+__device__ __forceinline__ uint32_t empty16(const uint4& v) {  // bit e set = entry e empty
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m |= ((w[i] & 0xFFFFu) == 0xFFFFu ? 1u : 0u) << (2 * i);
+    m |= ((w[i] >> 16) == 0xFFFFu ? 1u : 0u) << (2 * i + 1);
+  }
+  return m;
+}
+
+enum : uint32_t { kVisited = 0, kFresh = 1, kNoRoom = 2 };
+
+// Looks `id` up and, when absent and `may_insert`, inserts it.  Returns
+// kVisited, kFresh, or kNoRoom (absent and not insertable here).
+__device__ __forceinline__ uint32_t visit16(uint32_t* tab, uint32_t nb, float inv_nb, uint32_t id, bool may_insert) {
+  const Slot16 s1 = split16(mix24(id ^ 0x5A5A5Au), nb, inv_nb, 0);
+  const Slot16 s2 = split16(mix24(id ^ 0x3C3C3Cu), nb, inv_nb, 1);
+  unsigned short* t16 = reinterpret_cast<unsigned short*>(tab);
+  for (int attempt = 0; attempt < 4; ++attempt) {
+    const uint4 v1 = load_bucket(tab, s1.b), v2 = load_bucket(tab, s2.b);
+    if (holds16(v1, s1.tag) || holds16(v2, s2.tag)) return kVisited;
+    if (!may_insert) return kNoRoom;
+    const uint32_t e1 = empty16(v1), e2 = empty16(v2);
+    if ((e1 | e2) == 0) return kNoRoom;
+    const bool first = __popc(e1) >= __popc(e2);
+    uint32_t em = first ? e1 : e2;
+    const Slot16 c = first ? s1 : s2;
+    while (em) {
+      const uint32_t e = __ffs(em) - 1;
+      em &= em - 1;
+      const unsigned short old = atomicCAS(t16 + 8 * c.b + e, (unsigned short)0xFFFF, (unsigned short)c.tag);
+      if (old == 0xFFFF) return kFresh;
+    }
+  }
+  return kNoRoom;
 }
 
 // RaBitQ estimate of one record by one lane (all four chains on this lane).
@@ -236,8 +323,10 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
     if (lane == 0) {
       bdA[0] = md;
       biA[0] = ix.medoid;
-      htab[4 * hash_slot(ix.medoid, a.hcap >> 2)] = ix.medoid;
+      if (!a.vt16) htab[4 * hash_slot(ix.medoid, a.hcap >> 2)] = ix.medoid;
     }
+    __syncwarp();
+    if (a.vt16 && lane == 0) visit16(htab, a.hbuckets, a.inv_hbuckets, ix.medoid, true);
     __syncwarp();
     float* bd = bdA;
     uint32_t* bi = biA;
@@ -303,38 +392,55 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
       }
 
       // ---- visited filter (vamana.hh:172-182) ----
+      // Shared table first; ids it cannot hold go to this warp's spill table in
+      // global memory, which every later miss then consults.
       uint32_t m = 0;
       bool fresh[NPL];
 #pragma unroll
       for (int s = 0; s < NPL; ++s) {
         fresh[s] = false;
-        const uint32_t peers = __match_any_sync(kFull, nbr[s]);
-        const bool first = nbr[s] != kEmptySlot && (peers & lanemask_lt()) == 0;
-        if (!overflow && hcount + 32 > a.hlimit) {
-          overflow = gtab != nullptr;
+        const uint32_t id = nbr[s];
+        const uint32_t peers = __match_any_sync(kFull, id);
+        const bool first = id != kEmptySlot && (peers & lanemask_lt()) == 0;
+        const bool may_insert = hcount + 32 <= a.hlimit;
+        bool full = false;
+        if (first) {
+          const bool in_spill = overflow && table_contains(gtab, a.ovf_cap, id);
+          if (!in_spill) {
+            uint32_t r;
+            if (a.vt16) {
+              r = visit16(htab, a.hbuckets, a.inv_hbuckets, id, may_insert);
+            } else {
+              r = may_insert ? (bucket_insert(htab, a.hcap >> 2, id) ? kFresh : kVisited)
+                             : (bucket_contains(htab, a.hcap >> 2, id) ? kVisited : kNoRoom);
+            }
+            fresh[s] = r == kFresh;
+            full = r == kNoRoom;
+          }
+        }
+        const uint32_t need = __ballot_sync(kFull, full);
+        if (need) {
           if (!overflow) {
-            err |= kErrCapacity;
-          } else {
+            if (gtab == nullptr) {
+              err |= kErrCapacity;
+              break;
+            }
             uint4* g4 = reinterpret_cast<uint4*>(gtab);
             const uint4 e = make_uint4(kEmptySlot, kEmptySlot, kEmptySlot, kEmptySlot);
             for (uint32_t j = lane; j < (a.ovf_cap >> 2); j += 32) g4[j] = e;
             __syncwarp();
+            overflow = true;
           }
-        }
-        if (overflow && gcount + 32 > a.ovf_limit) err |= kErrCapacity;
-        if (err & kErrCapacity) break;
-        if (first) {
-          if (!overflow)
-            fresh[s] = bucket_insert(htab, a.hcap >> 2, nbr[s]);
-          else
-            fresh[s] = !bucket_contains(htab, a.hcap >> 2, nbr[s]) && table_insert(gtab, a.ovf_cap, nbr[s]);
+          if (gcount + 32 > a.ovf_limit) {
+            err |= kErrCapacity;
+            break;
+          }
+          if (full) fresh[s] = table_insert(gtab, a.ovf_cap, id);
+          gcount += __popc(__ballot_sync(kFull, full && fresh[s]));
         }
         const uint32_t cnt = __popc(__ballot_sync(kFull, fresh[s]));
         m += cnt;
-        if (overflow)
-          gcount += cnt;
-        else
-          hcount += cnt;
+        hcount += cnt;
       }
       if (err & kErrCapacity) break;
       if (m == 0) {
