@@ -29,6 +29,7 @@ EXPORTED = (
     "dvs_set_hop_limit", "dvs_set_visited_slots", "dvs_query_prepare", "dvs_rabitq_estimate", "dvs_l2_distances", "dvs_host_index_load",
     "dvs_host_index_info", "dvs_host_index_arrays", "dvs_host_index_free", "dvs_write_index", "dvs_last_error",
     "dvs_status_string", "dvs_device_count", "dvs_build_index", "dvs_set_kernel_timing", "dvs_kernel_times",
+    "dvs_search_device_noalloc",
 )
 
 
@@ -82,6 +83,7 @@ def lib():
             "dvs_index_download": [vp, vp, vp, vp, vp],
             "dvs_search": [vp, vp, u32, u32, u32, u32, i32, vp, vp, C.POINTER(Stats)],
             "dvs_search_device": [vp, u32, vp, u32, u32, u32, u32, i32, vp, vp, vp, vp],
+            "dvs_search_device_noalloc": [vp, u32, vp, u32, u32, u32, u32, i32, vp, vp, vp, vp],
             "dvs_set_hop_limit": [vp, u32],
             "dvs_set_visited_slots": [vp, u32],
             "dvs_set_kernel_timing": [vp, i32],

@@ -593,3 +593,39 @@ dvs_status dvs_l2_distances(const float* d_query, const float* d_candidates, flo
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Read-only views for entry points defined in other translation units.
+// ---------------------------------------------------------------------------
+namespace dvs {
+
+dvs_status device_view(dvs_index* ix, uint32_t slot, DeviceView* out) {
+  if (!ix || !out) return fail(DVS_ERR_ARG, "null argument");
+  if (slot >= ix->devs.size()) return fail(DVS_ERR_ARG, "device slot out of range");
+  const Device& d = ix->devs[slot];
+  out->lay = d.lay;
+  out->ordinal = d.ordinal;
+  out->sm_count = d.sm_count;
+  out->stream = d.stream;
+  out->hop_limit = ix->hop_limit;
+  out->index_dim = ix->host.info.dim;
+  return DVS_OK;
+}
+
+dvs_status search_shape(dvs_index* ix, uint32_t slot, uint32_t cap, SearchShape* out) {
+  if (!ix || !out || slot >= ix->devs.size()) return fail(DVS_ERR_ARG, "bad argument");
+  LaunchShape s;
+  const dvs_status rc = launch_shape(ix->devs[slot], cap, ix->slots_per_entry, s);
+  if (rc != DVS_OK) return rc;
+  out->cap = s.cap;
+  out->cap_pad = s.cap_pad;
+  out->hcap = s.hcap;
+  out->hlimit = s.hlimit;
+  out->vt16 = s.vt16;
+  out->hbuckets = s.hbuckets;
+  out->wpb = s.wpb;
+  out->blocks_per_sm = s.blocks_per_sm;
+  return DVS_OK;
+}
+
+}  // namespace dvs

@@ -5,6 +5,8 @@
 
 #include <cstdint>
 
+#include "dvs_b200.h"
+
 namespace dvs {
 
 // Device layout of one index copy (dense slot order).
@@ -44,6 +46,21 @@ struct SearchArgs {
   uint32_t cap_pad = 0, dim_pad = 0;
 };
 
+// What another translation unit may read of an open index's device copy.
+struct DeviceView {
+  DevLayout lay;
+  int ordinal = 0;
+  uint32_t sm_count = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t hop_limit = 0;
+  uint32_t index_dim = 0;
+};
+
+// Launch shape of the search kernel for one beam capacity.
+struct SearchShape {
+  uint32_t cap = 0, cap_pad = 0, hcap = 0, hlimit = 0, vt16 = 0, hbuckets = 0, wpb = 0, blocks_per_sm = 0;
+};
+
 constexpr uint32_t kErrCapacity = 1u;
 constexpr uint32_t kErrHopLimit = 2u;
 
@@ -64,6 +81,13 @@ cudaError_t launch_search(const SearchArgs& a, uint32_t warps_per_block, uint32_
 // per-warp shared memory; also sets the kernel's dynamic smem attribute.
 cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, uint32_t warps_per_block, size_t smem_bytes,
                              int* blocks_per_sm);
+
+}  // namespace dvs
+
+struct dvs_index;
+namespace dvs {
+dvs_status device_view(dvs_index* ix, uint32_t slot, DeviceView* out);
+dvs_status search_shape(dvs_index* ix, uint32_t slot, uint32_t cap, SearchShape* out);
 
 cudaError_t launch_estimate_ref_layout(const float* qrot, const float* f3, const uint8_t* records, float* out,
                                        uint32_t n, uint32_t dim, uint32_t bits, cudaStream_t stream);

@@ -131,13 +131,28 @@ dvs_status dvs_search_device(dvs_index* index, uint32_t device_slot, const float
                              uint32_t dim, uint32_t k, uint32_t beam_width, dvs_mode mode, uint32_t* d_out_ids,
                              float* d_out_dist, uint32_t* d_counters, void* stream);
 
+/* dvs_search_device without any device allocation, for callers that may not
+ * call cudaMalloc once running (a serving engine that has reserved the GPU's
+ * free memory for its own pool, a request path where allocation is
+ * forbidden).  No counterpart in the reference.  Same arguments and results
+ * as dvs_search_device; the scratch (rotated queries, factors, work counters,
+ * visited-set spill tables) comes from one fixed 16 MiB __device__ array per
+ * GPU instead of cudaMalloc, which caps a call at
+ * 8 MiB / (4*round_up(dim,4) + 16) queries (20,971 at dim 96; more returns
+ * DVS_ERR_CAPACITY).  The first call on a device looks the array up with
+ * cudaGetSymbolAddress; make it before any stream capture.  Calls share the
+ * array: calls whose work overlaps on the GPU race and must be serialised. */
+dvs_status dvs_search_device_noalloc(dvs_index* index, uint32_t device_slot, const float* d_queries, uint32_t nq,
+                                     uint32_t dim, uint32_t k, uint32_t beam_width, dvs_mode mode,
+                                     uint32_t* d_out_ids, float* d_out_dist, uint32_t* d_counters, void* stream);
+
 /* Expansion cap per query (0 = none, the reference's behaviour).  A query that
  * reaches it stops expanding, still reranks, and makes the search return
  * DVS_ERR_HOP_LIMIT. */
 dvs_status dvs_set_hop_limit(dvs_index* index, uint32_t max_expansions);
 
-/* Shared-memory visited-set size in slots per beam entry (default 64 for
- * indexes of fewer than 2^24 nodes use 16-bit entries, larger ones 32-bit).  A
+/* Shared-memory visited-set size in slots per beam entry (default 48; indexes
+ * of fewer than 2^24 nodes use 16-bit entries, larger ones 32-bit).  A
  * query whose visited set outgrows it continues in a per-warp global-memory
  * table with identical results; smaller values trade shared memory (and
  * therefore more resident queries per SM) for spills.  Valid range 2..256;
