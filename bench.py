@@ -43,7 +43,7 @@ PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "search_kernel_gauss-1m-d96.txt
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default=WORKLOAD)
@@ -134,19 +134,26 @@ def clocks_sampler(device):
          "clocks_event_reasons.sw_power_cap")
     try:
         p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-i", str(device),
-                              "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                              "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
     except OSError:
         return None
     lines = []
-    th = threading.Thread(target=lambda: lines.extend(p.stdout), daemon=True)
+
+    def reader():
+        for ln in p.stdout:
+            lines.append((time.time(), ln))
+
+    th = threading.Thread(target=reader, daemon=True)
     th.start()
+    time.sleep(0.5)  # nvidia-smi needs a moment before its first sample
     return p, lines, th
 
 
-def clocks_summary(sampler):
+def clocks_summary(sampler, t0=None, t1=None):
+    """Median SM clock and throttle reasons of the samples taken in [t0, t1]."""
     if sampler is None:
         return None
-    p, lines, th = sampler
+    p, stamped, th = sampler
     p.terminate()
     try:
         p.wait(timeout=5)
@@ -155,7 +162,8 @@ def clocks_summary(sampler):
     th.join(timeout=2)
     sm, mx, reasons = [], [], set()
     names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-    for ln in lines:
+    inside = [ln for ts, ln in stamped if t0 is None or t0 - 0.06 <= ts <= t1 + 0.06]
+    for ln in inside:
         f = [x.strip() for x in ln.split(",")]
         if len(f) < 9:
             continue
@@ -320,18 +328,20 @@ def run_ours(args):
     torch.cuda.synchronize(device)
     ix.set_kernel_timing(True)
     ix.kernel_times()
+    sampler = clocks_sampler(device)
     dist.barrier()
     torch.cuda.synchronize(device)
-    sampler = clocks_sampler(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
     e0.record(stream)
     for s in range(args.steps):
         ix.search_device(dq[args.warmup + s], k, L, d_out_ids=out_ids, d_out_dist=out_d, d_counters=cnt,
                          stream=stream)
     e1.record(stream)
     torch.cuda.synchronize(device)
+    t_wall1 = time.time()
     dist.barrier()
-    clocks = clocks_summary(sampler)
+    clocks = clocks_summary(sampler, t_wall0, t_wall1)
     ms = e0.elapsed_time(e1)
     n_search, prep_ms, search_ms = ix.kernel_times()
     ix.set_kernel_timing(False)
