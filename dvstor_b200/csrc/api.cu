@@ -48,6 +48,8 @@ struct Device {
   cudaStream_t stream = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   uint32_t sm_count = 0;
+  uint32_t shard = 0;     // shard held (sharded placement), rows = its row count
+  uint64_t rows = 0;
   // index
   uint32_t* adj = nullptr;
   uint32_t* rec = nullptr;
@@ -105,9 +107,12 @@ struct LaunchShape {
   uint32_t vt16 = 0, hbuckets = 0, hlimit = 0;
 };
 
-dvs_status upload(Device& d, const HostIndex& h) {
+// Uploads the rows of shard `shard` of `nshard` (slot g with g mod nshard ==
+// shard, local row g / nshard; nshard == 1 uploads everything).
+dvs_status upload(Device& d, const HostIndex& h, uint32_t shard, uint32_t nshard) {
   const dvs_index_info& in = h.info;
   const uint64_t n = in.num_vectors;
+  const uint64_t nl = (n + nshard - 1 - shard) / nshard;
   const uint32_t dim = in.dim, R = in.R, bits = in.rabitq_bits;
   const uint32_t packed = (bits * dim + 7) / 8;
   const uint32_t code_words = (packed + 3) / 4;
@@ -121,33 +126,33 @@ dvs_status upload(Device& d, const HostIndex& h) {
   DVS_CUDA(cudaEventCreate(&d.ev0));
   DVS_CUDA(cudaEventCreate(&d.ev1));
   // records: reference layout -> [codes | pad to word | add | rescale | pad to 16 B]
-  std::vector<uint32_t> rec(size_t(n) * rec_words, 0u);
-  for (uint64_t g = 0; g < n; ++g) {
+  std::vector<uint32_t> rec(size_t(nl) * rec_words, 0u);
+  std::vector<uint32_t> adj(size_t(nl) * R);
+  std::vector<float> vecs(size_t(nl) * vec_stride, 0.f);
+  for (uint64_t l = 0; l < nl; ++l) {
+    const uint64_t g = l * nshard + shard;
     const uint8_t* src = h.records.data() + g * in.rabitq_size;
-    uint8_t* dst = reinterpret_cast<uint8_t*>(rec.data() + g * rec_words);
+    uint8_t* dst = reinterpret_cast<uint8_t*>(rec.data() + l * rec_words);
     std::memcpy(dst, src, packed);
     std::memcpy(dst + size_t(code_words) * 4, src + packed, 8);
+    std::memcpy(&adj[l * R], &h.adj[g * R], size_t(R) * 4);
+    std::memcpy(&vecs[l * vec_stride], &h.vecs[g * dim], size_t(dim) * 4);
   }
-  std::vector<float> vecs;
-  const float* vsrc = h.vecs.data();
-  if (vec_stride != dim) {
-    vecs.assign(size_t(n) * vec_stride, 0.f);
-    for (uint64_t g = 0; g < n; ++g) std::memcpy(&vecs[g * vec_stride], &h.vecs[g * dim], size_t(dim) * 4);
-    vsrc = vecs.data();
-  }
-  DVS_CUDA(cudaMalloc(&d.adj, size_t(n) * R * 4));
+  DVS_CUDA(cudaMalloc(&d.adj, adj.size() * 4));
   DVS_CUDA(cudaMalloc(&d.rec, rec.size() * 4));
-  DVS_CUDA(cudaMalloc(&d.vecs, size_t(n) * vec_stride * 4));
+  DVS_CUDA(cudaMalloc(&d.vecs, vecs.size() * 4));
   DVS_CUDA(cudaMalloc(&d.ids, size_t(n) * 4));
   DVS_CUDA(cudaMalloc(&d.P, size_t(dim) * dim * 4));
   DVS_CUDA(cudaMalloc(&d.c_rot, size_t(dim) * 4));
-  DVS_CUDA(cudaMemcpy(d.adj, h.adj.data(), size_t(n) * R * 4, cudaMemcpyHostToDevice));
+  DVS_CUDA(cudaMemcpy(d.adj, adj.data(), adj.size() * 4, cudaMemcpyHostToDevice));
   DVS_CUDA(cudaMemcpy(d.rec, rec.data(), rec.size() * 4, cudaMemcpyHostToDevice));
-  DVS_CUDA(cudaMemcpy(d.vecs, vsrc, size_t(n) * vec_stride * 4, cudaMemcpyHostToDevice));
+  DVS_CUDA(cudaMemcpy(d.vecs, vecs.data(), vecs.size() * 4, cudaMemcpyHostToDevice));
   DVS_CUDA(cudaMemcpy(d.ids, h.ids.data(), size_t(n) * 4, cudaMemcpyHostToDevice));
   DVS_CUDA(cudaMemcpy(d.P, h.rotation.data(), size_t(dim) * dim * 4, cudaMemcpyHostToDevice));
   DVS_CUDA(cudaMemcpy(d.c_rot, h.rotated_centroid.data(), size_t(dim) * 4, cudaMemcpyHostToDevice));
   DVS_CUDA(cudaMalloc(&d.work, 16));
+  d.shard = shard;
+  d.rows = nl;
   DevLayout& L = d.lay;
   L.adj = d.adj;
   L.rec = d.rec;
@@ -164,6 +169,42 @@ dvs_status upload(Device& d, const HostIndex& h) {
   L.rec_words = rec_words;
   L.code_words = code_words;
   L.vec_stride = vec_stride;
+  L.adj_s[0] = d.adj;
+  L.rec_s[0] = d.rec;
+  L.vecs_s[0] = d.vecs;
+  return DVS_OK;
+}
+
+// Sharded placement: every device may read every other device's shard.
+dvs_status link_shards(std::vector<Device>& devs) {
+  const uint32_t ns = uint32_t(devs.size());
+  for (uint32_t i = 0; i < ns; ++i) {
+    for (uint32_t j = 0; j < ns; ++j) {
+      if (devs[i].ordinal == devs[j].ordinal) continue;
+      int can = 0;
+      DVS_CUDA(cudaDeviceCanAccessPeer(&can, devs[i].ordinal, devs[j].ordinal));
+      if (!can)
+        return fail(DVS_ERR_PEER, "device " + std::to_string(devs[i].ordinal) + " cannot access device " +
+                                      std::to_string(devs[j].ordinal) + "'s memory; open the index replicated");
+      DVS_CUDA(cudaSetDevice(devs[i].ordinal));
+      const cudaError_t e = cudaDeviceEnablePeerAccess(devs[j].ordinal, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled)
+        cudaGetLastError();
+      else if (e != cudaSuccess)
+        return fail(DVS_ERR_PEER, std::string("cudaDeviceEnablePeerAccess: ") + cudaGetErrorString(e));
+    }
+  }
+  uint32_t log = 0;
+  while ((1u << log) < ns) ++log;
+  for (auto& d : devs) {
+    d.lay.shard_log = log;
+    d.lay.shard_mask = ns - 1;
+    for (uint32_t s = 0; s < ns; ++s) {
+      d.lay.adj_s[s] = devs[s].adj;
+      d.lay.rec_s[s] = devs[s].rec;
+      d.lay.vecs_s[s] = devs[s].vecs;
+    }
+  }
   return DVS_OK;
 }
 
@@ -348,8 +389,8 @@ int dvs_device_count(void) {
 dvs_status dvs_open(const dvs_open_params* p, dvs_index** out) {
   if (!p || !out || !p->index_prefix) return fail(DVS_ERR_ARG, "null argument");
   *out = nullptr;
-  if (p->placement != DVS_PLACE_REPLICATE)
-    return fail(DVS_ERR_UNSUPPORTED, "only replicated placement is available in this build");
+  if (p->placement != DVS_PLACE_REPLICATE && p->placement != DVS_PLACE_SHARD)
+    return fail(DVS_ERR_ARG, "placement must be DVS_PLACE_REPLICATE or DVS_PLACE_SHARD");
   const int ndev_vis = dvs_device_count();
   if (ndev_vis == 0) return fail(DVS_ERR_NO_DEVICE, "no CUDA device is visible");
   std::vector<int> devs;
@@ -373,12 +414,22 @@ dvs_status dvs_open(const dvs_open_params* p, dvs_index** out) {
     s = fail(DVS_ERR_FORMAT, "RaBitQ artifact memory-node count mismatch: expected " +
                                  std::to_string(p->expect_memory_nodes) + ", got " +
                                  std::to_string(in.num_memory_nodes));
+  const bool sharded = p->placement == DVS_PLACE_SHARD && devs.size() > 1;
+  if (s == DVS_OK && sharded) {
+    const size_t ns = devs.size();
+    if (ns > dvs::kMaxShards || (ns & (ns - 1)) != 0)
+      s = fail(DVS_ERR_ARG, "sharded placement needs a power-of-two device count up to 16");
+    else if (in.num_vectors < ns)
+      s = fail(DVS_ERR_ARG, "fewer nodes than shards");
+  }
   if (s == DVS_OK) {
     ix->devs.resize(devs.size());
     for (size_t i = 0; i < devs.size() && s == DVS_OK; ++i) {
       ix->devs[i].ordinal = devs[i];
-      s = dvs::upload(ix->devs[i], ix->host);
+      s = sharded ? dvs::upload(ix->devs[i], ix->host, uint32_t(i), uint32_t(devs.size()))
+                  : dvs::upload(ix->devs[i], ix->host, 0, 1);
     }
+    if (s == DVS_OK && sharded) s = dvs::link_shards(ix->devs);
   }
   if (s != DVS_OK) {
     for (auto& d : ix->devs) d.release();
@@ -453,25 +504,32 @@ dvs_status dvs_kernel_times(dvs_index* ix, uint32_t slot, uint32_t* searches, do
 dvs_status dvs_index_download(const dvs_index* ix, uint32_t* h_adj, uint8_t* h_records, float* h_vecs,
                               uint32_t* h_ids) {
   if (!ix || ix->devs.empty()) return fail(DVS_ERR_ARG, "null index");
-  const dvs::Device& d = ix->devs[0];
-  const dvs::DevLayout& L = d.lay;
-  const uint64_t n = L.n;
-  DVS_CUDA(cudaSetDevice(d.ordinal));
-  if (h_adj) DVS_CUDA(cudaMemcpy(h_adj, d.adj, size_t(n) * L.R * 4, cudaMemcpyDeviceToHost));
-  if (h_ids) DVS_CUDA(cudaMemcpy(h_ids, d.ids, size_t(n) * 4, cudaMemcpyDeviceToHost));
-  if (h_vecs) {
-    std::vector<float> v(size_t(n) * L.vec_stride);
-    DVS_CUDA(cudaMemcpy(v.data(), d.vecs, v.size() * 4, cudaMemcpyDeviceToHost));
-    for (uint64_t g = 0; g < n; ++g) std::memcpy(h_vecs + g * L.dim, &v[g * L.vec_stride], size_t(L.dim) * 4);
+  const dvs::DevLayout& L0 = ix->devs[0].lay;
+  const uint32_t ns = L0.shard_log == 0 ? 1u : uint32_t(ix->devs.size());
+  if (h_ids) {
+    DVS_CUDA(cudaSetDevice(ix->devs[0].ordinal));
+    DVS_CUDA(cudaMemcpy(h_ids, ix->devs[0].ids, size_t(L0.n) * 4, cudaMemcpyDeviceToHost));
   }
-  if (h_records) {
-    const uint32_t packed = (L.bits * L.dim + 7) / 8, rs = packed + 8;
-    std::vector<uint32_t> r(size_t(n) * L.rec_words);
+  for (uint32_t sh = 0; sh < ns; ++sh) {
+    const dvs::Device& d = ix->devs[sh];
+    const dvs::DevLayout& L = d.lay;
+    const uint64_t nl = d.rows;
+    DVS_CUDA(cudaSetDevice(d.ordinal));
+    std::vector<uint32_t> a(size_t(nl) * L.R), r(size_t(nl) * L.rec_words);
+    std::vector<float> v(size_t(nl) * L.vec_stride);
+    DVS_CUDA(cudaMemcpy(a.data(), d.adj, a.size() * 4, cudaMemcpyDeviceToHost));
     DVS_CUDA(cudaMemcpy(r.data(), d.rec, r.size() * 4, cudaMemcpyDeviceToHost));
-    for (uint64_t g = 0; g < n; ++g) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(r.data() + g * L.rec_words);
-      std::memcpy(h_records + g * rs, src, packed);
-      std::memcpy(h_records + g * rs + packed, src + size_t(L.code_words) * 4, 8);
+    DVS_CUDA(cudaMemcpy(v.data(), d.vecs, v.size() * 4, cudaMemcpyDeviceToHost));
+    const uint32_t packed = (L.bits * L.dim + 7) / 8, rs = packed + 8;
+    for (uint64_t l = 0; l < nl; ++l) {
+      const uint64_t g = l * ns + sh;
+      if (h_adj) std::memcpy(h_adj + g * L.R, &a[l * L.R], size_t(L.R) * 4);
+      if (h_vecs) std::memcpy(h_vecs + g * L.dim, &v[l * L.vec_stride], size_t(L.dim) * 4);
+      if (h_records) {
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(r.data() + l * L.rec_words);
+        std::memcpy(h_records + g * rs, src, packed);
+        std::memcpy(h_records + g * rs + packed, src + size_t(L.code_words) * 4, 8);
+      }
     }
   }
   return DVS_OK;

@@ -186,7 +186,7 @@ template <int BITS>
 __device__ __forceinline__ float estimate_lane(const DevLayout& ix, uint32_t c, const float* __restrict__ qr,
                                                float q_add, float q_k1) {
   constexpr int kPer = 32 / BITS;
-  const uint4* r = reinterpret_cast<const uint4*>(ix.rec) + size_t(c) * (ix.rec_words >> 2);
+  const uint4* r = reinterpret_cast<const uint4*>(rec_row(ix, c));
   const uint32_t nch = (ix.code_words + 2 + 3) >> 2;
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, add_o = 0.f, rs_o = 0.f;
   for (uint32_t c0 = 0; c0 < nch; c0 += 8) {
@@ -225,7 +225,7 @@ __device__ __forceinline__ void l2_rows_warp(const DevLayout& ix, const float* _
     float part = 0.f;
     if (i < count) {
       const uint32_t row = rows[i] & row_mask;
-      part = l2_quad_partial(q, ix.vecs + size_t(row) * ix.vec_stride, ix.dim, t);
+      part = l2_quad_partial(q, vec_row(ix, row), ix.dim, t);
     }
     const float total = quad_butterfly(part);
     if (i < count && t == 0) out[i] = total;
@@ -292,9 +292,7 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
   uint32_t* gtab = a.ovf ? a.ovf + size_t(warp_slot) * a.ovf_cap : nullptr;
   const bool rabitq = a.mode == 0;
   const uint32_t dim = ix.dim, R = ix.R;
-  const uint32_t rec_stride4 = ix.rec_words >> 2;
   const uint32_t nch = (ix.code_words + 2 + 3) >> 2;
-  const uint4* rec4 = reinterpret_cast<const uint4*>(ix.rec);
   const float kInf = __int_as_float(0x7F800000);
 
   for (;;) {
@@ -319,7 +317,7 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
       for (uint32_t j = lane; j < (a.hcap >> 2); j += 32) h4[j] = e;
     }
     __syncwarp();
-    const float md = seed_distance_warp(qv, ix.vecs + size_t(ix.medoid) * ix.vec_stride, dim, ix.metric == 1, lane);
+    const float md = seed_distance_warp(qv, vec_row(ix, ix.medoid), dim, ix.metric == 1, lane);
     if (lane == 0) {
       bdA[0] = md;
       biA[0] = ix.medoid;
@@ -369,13 +367,13 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
 #pragma unroll
       for (int s = 0; s < NPL; ++s) {
         const uint32_t j = lane + 32u * s;
-        nbr[s] = hit ? pf[s] : (j < R ? __ldg(ix.adj + size_t(u) * R + j) : kEmptySlot);
+        nbr[s] = hit ? pf[s] : (j < R ? __ldg(adj_row(ix, u) + j) : kEmptySlot);
       }
       pf_node = guess;
 #pragma unroll
       for (int s = 0; s < NPL; ++s) {
         const uint32_t j = lane + 32u * s;
-        pf[s] = (guess != kEmptySlot && j < R) ? __ldg(ix.adj + size_t(guess) * R + j) : kEmptySlot;
+        pf[s] = (guess != kEmptySlot && j < R) ? __ldg(adj_row(ix, guess) + j) : kEmptySlot;
       }
       // records of every listed neighbour are requested before the visited
       // check so their latency overlaps it; visited ones are discarded
@@ -386,7 +384,7 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
           if (nbr[s] != kEmptySlot) {
 #pragma unroll
             for (int c = 0; c < RCH; ++c)
-              if (c < int(nch)) rv[s][c] = __ldg(rec4 + size_t(nbr[s]) * rec_stride4 + c);
+              if (c < int(nch)) rv[s][c] = __ldg(reinterpret_cast<const uint4*>(rec_row(ix, nbr[s])) + c);
           }
         }
       }

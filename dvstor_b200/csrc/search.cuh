@@ -15,17 +15,39 @@ namespace dvs {
 //            f32 add | f32 rescale | zero pad to a 16-byte multiple]
 //   vecs     n rows of vec_stride floats (dim, zero-padded to a multiple of 4)
 //   ids      n u32 node ids as stored in the shards
+constexpr uint32_t kMaxShards = 16;
+
 struct DevLayout {
-  const uint32_t* adj = nullptr;
+  // Node g lives in shard (g & shard_mask) at local row (g >> shard_log); a
+  // replicated layout is one shard.  Shard arrays of other devices are peer
+  // pointers (NVLink).
+  const uint32_t* adj_s[kMaxShards] = {};
+  const uint32_t* rec_s[kMaxShards] = {};
+  const float* vecs_s[kMaxShards] = {};
+  uint32_t shard_log = 0, shard_mask = 0;
+  const uint32_t* adj = nullptr;    // shard 0 (the whole index when replicated)
   const uint32_t* rec = nullptr;
   const float* vecs = nullptr;
-  const uint32_t* ids = nullptr;
+  const uint32_t* ids = nullptr;    // replicated: every node's stored id
   const float* P = nullptr;         // dim*dim column-major rotation
   const float* c_rot = nullptr;     // rotated centroid
   uint64_t n = 0;
   uint32_t dim = 0, R = 0, bits = 0, medoid = 0, metric = 0;
   uint32_t rec_words = 0, code_words = 0, vec_stride = 0;
 };
+
+__device__ __forceinline__ const uint32_t* adj_row(const DevLayout& ix, uint32_t g) {
+  if (ix.shard_log == 0) return ix.adj + size_t(g) * ix.R;
+  return ix.adj_s[g & ix.shard_mask] + size_t(g >> ix.shard_log) * ix.R;
+}
+__device__ __forceinline__ const uint32_t* rec_row(const DevLayout& ix, uint32_t g) {
+  if (ix.shard_log == 0) return ix.rec + size_t(g) * ix.rec_words;
+  return ix.rec_s[g & ix.shard_mask] + size_t(g >> ix.shard_log) * ix.rec_words;
+}
+__device__ __forceinline__ const float* vec_row(const DevLayout& ix, uint32_t g) {
+  if (ix.shard_log == 0) return ix.vecs + size_t(g) * ix.vec_stride;
+  return ix.vecs_s[g & ix.shard_mask] + size_t(g >> ix.shard_log) * ix.vec_stride;
+}
 
 struct SearchArgs {
   DevLayout ix;
