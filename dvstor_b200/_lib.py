@@ -29,7 +29,7 @@ EXPORTED = (
     "dvs_set_hop_limit", "dvs_set_visited_slots", "dvs_query_prepare", "dvs_rabitq_estimate", "dvs_l2_distances", "dvs_host_index_load",
     "dvs_host_index_info", "dvs_host_index_arrays", "dvs_host_index_free", "dvs_write_index", "dvs_last_error",
     "dvs_status_string", "dvs_device_count", "dvs_build_index", "dvs_set_kernel_timing", "dvs_kernel_times",
-    "dvs_search_device_noalloc",
+    "dvs_search_device_noalloc", "dvs_set_rotation", "dvs_query_prepare_tc",
 )
 
 
@@ -89,6 +89,8 @@ def lib():
             "dvs_set_kernel_timing": [vp, i32],
             "dvs_kernel_times": [vp, u32, C.POINTER(u32), C.POINTER(C.c_double), C.POINTER(C.c_double)],
             "dvs_query_prepare": [vp, vp, vp, vp, vp, u32, u32, u32, vp],
+            "dvs_query_prepare_tc": [vp, vp, vp, vp, vp, u32, u32, u32, vp],
+            "dvs_set_rotation": [vp, i32],
             "dvs_rabitq_estimate": [vp, vp, vp, vp, u32, u32, u32, vp],
             "dvs_l2_distances": [vp, vp, vp, u32, u32, vp],
             "dvs_host_index_load": [C.c_char_p, C.POINTER(vp)],

@@ -281,6 +281,7 @@ struct dvs_index {
   uint32_t hop_limit = 0;
   uint32_t slots_per_entry = 0;  // 0 = the default of the table kind in use
   bool kernel_timing = false;
+  dvs_rotation rotation = DVS_ROTATION_EXACT;
   std::mutex mu;
 };
 
@@ -323,8 +324,12 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
   if (timed) DVS_CUDA(cudaEventRecord(d.ev0, st));
   if (tr) DVS_CUDA(cudaEventRecord(tr[0], st));
   if (rabitq) {
-    DVS_CUDA(launch_prepare(d_q, lay.dim, lay.P, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits, nq,
-                            st));
+    if (ix->rotation == DVS_ROTATION_TENSOR)
+      DVS_CUDA(launch_prepare_tc(d_q, lay.dim, lay.P, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits,
+                                 nq, d.work + 1, st));
+    else
+      DVS_CUDA(launch_prepare(d_q, lay.dim, lay.P, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits, nq,
+                              st));
   }
   if (tr) DVS_CUDA(cudaEventRecord(tr[1], st));
   SearchArgs a;
@@ -472,6 +477,14 @@ dvs_status dvs_set_visited_slots(dvs_index* ix, uint32_t slots_per_beam_entry) {
   return DVS_OK;
 }
 
+dvs_status dvs_set_rotation(dvs_index* ix, dvs_rotation rotation) {
+  if (!ix) return fail(DVS_ERR_ARG, "null index");
+  if (rotation != DVS_ROTATION_EXACT && rotation != DVS_ROTATION_TENSOR) return fail(DVS_ERR_ARG, "unknown rotation");
+  std::lock_guard<std::mutex> g(ix->mu);
+  ix->rotation = rotation;
+  return DVS_OK;
+}
+
 dvs_status dvs_set_kernel_timing(dvs_index* ix, int enable) {
   if (!ix) return fail(DVS_ERR_ARG, "null index");
   std::lock_guard<std::mutex> g(ix->mu);
@@ -596,6 +609,8 @@ dvs_status dvs_search(dvs_index* ix, const float* h_queries, uint32_t nq, uint32
         return fail(DVS_ERR_CAPACITY, "a query's visited set exceeded its capacity; its results are partial");
       if (work[1] & dvs::kErrHopLimit)
         return fail(DVS_ERR_HOP_LIMIT, "a query reached the expansion limit; its results are partial");
+      if (work[1] & dvs::kErrTimeout)
+        return fail(DVS_ERR_TIMEOUT, "the tensor-core rotation gave up waiting for its MMAs");
       return DVS_OK;
     };
     st[i] = body();
@@ -629,6 +644,26 @@ dvs_status dvs_query_prepare(const float* d_query, const float* d_P, const float
   if (dim == 0) return fail(DVS_ERR_DIM, "dim must be > 0");
   DVS_CUDA(dvs::launch_prepare(d_query, dim, d_P, d_centroid, d_rot_query, dim, d_factor, 3, dim, bits, nq,
                                static_cast<cudaStream_t>(stream)));
+  return DVS_OK;
+}
+
+dvs_status dvs_query_prepare_tc(const float* d_query, const float* d_P, const float* d_centroid, float* d_rot_query,
+                                float* d_factor, uint32_t nq, uint32_t dim, uint32_t bits, void* stream) {
+  if (!d_query || !d_P || !d_centroid || !d_rot_query || !d_factor) return fail(DVS_ERR_ARG, "null buffer");
+  if (bits != 1 && bits != 2 && bits != 4 && bits != 8) return fail(DVS_ERR_BITS, "bits must be 1, 2, 4, or 8");
+  if (dim == 0) return fail(DVS_ERR_DIM, "dim must be > 0");
+  if (nq == 0) return DVS_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* d_err = nullptr;
+  DVS_CUDA(cudaMallocAsync(&d_err, 4, st));
+  DVS_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
+  DVS_CUDA(dvs::launch_prepare_tc(d_query, dim, d_P, d_centroid, d_rot_query, dim, d_factor, 3, dim, bits, nq, d_err,
+                                  st));
+  uint32_t h_err = 0;
+  DVS_CUDA(cudaMemcpyAsync(&h_err, d_err, 4, cudaMemcpyDeviceToHost, st));
+  DVS_CUDA(cudaFreeAsync(d_err, st));
+  DVS_CUDA(cudaStreamSynchronize(st));
+  if (h_err & dvs::kErrTimeout) return fail(DVS_ERR_TIMEOUT, "the tensor-core rotation gave up waiting for its MMAs");
   return DVS_OK;
 }
 

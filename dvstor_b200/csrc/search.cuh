@@ -85,6 +85,7 @@ struct SearchShape {
 
 constexpr uint32_t kErrCapacity = 1u;
 constexpr uint32_t kErrHopLimit = 2u;
+constexpr uint32_t kErrTimeout = 4u;
 
 // Words of shared memory one warp of the search kernel uses.
 __host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap) {
@@ -94,6 +95,12 @@ __host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t
 cudaError_t launch_prepare(const float* queries, uint32_t q_stride, const float* P, const float* c_rot, float* qrot,
                            uint32_t qrot_stride, float* qfac, uint32_t fac_stride, uint32_t dim, uint32_t bits,
                            uint32_t nq, cudaStream_t stream);
+
+// Q' = Q P^T on tcgen05 tensor cores (3xTF32) plus the query factors; a
+// bounded mbarrier wait that expires ORs kErrTimeout into *err.
+cudaError_t launch_prepare_tc(const float* queries, uint32_t q_stride, const float* P, const float* c_rot, float* qrot,
+                              uint32_t qrot_stride, float* qfac, uint32_t fac_stride, uint32_t dim, uint32_t bits,
+                              uint32_t nq, uint32_t* err, cudaStream_t stream);
 
 // Launches the persistent search kernel; warps_per_block and blocks come from
 // the caller's occupancy computation.

@@ -60,6 +60,10 @@ class Index:
     def set_hop_limit(self, max_expansions: int) -> None:
         check(lib().dvs_set_hop_limit(self._h, max_expansions))
 
+    def set_rotation(self, rotation: str) -> None:
+        """'exact' (fp32 FMA chains, the default) or 'tensor' (tcgen05, 3xTF32)."""
+        check(lib().dvs_set_rotation(self._h, {"exact": 0, "tensor": 1}[rotation]))
+
     def set_kernel_timing(self, enable: bool) -> None:
         check(lib().dvs_set_kernel_timing(self._h, 1 if enable else 0))
 

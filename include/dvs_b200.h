@@ -146,6 +146,14 @@ dvs_status dvs_search_device_noalloc(dvs_index* index, uint32_t device_slot, con
                                      uint32_t dim, uint32_t k, uint32_t beam_width, dvs_mode mode,
                                      uint32_t* d_out_ids, float* d_out_dist, uint32_t* d_counters, void* stream);
 
+/* How the query rotation q' = P^T q is computed (src/gpu/gpu_kernel_launcher.cu
+ * :289-297 uses cublasSgemv).  EXACT: fp32 FMA chains in a fixed order (the
+ * default; results equal the CPU oracle's bit for bit).  TENSOR: tcgen05 MMAs
+ * with the 3xTF32 split, fp32 accuracy (~1e-6 relative) at tensor-core speed;
+ * the rotated query then differs from the fixed order in the last bits. */
+typedef enum dvs_rotation { DVS_ROTATION_EXACT = 0, DVS_ROTATION_TENSOR = 1 } dvs_rotation;
+dvs_status dvs_set_rotation(dvs_index* index, dvs_rotation rotation);
+
 /* Expansion cap per query (0 = none, the reference's behaviour).  A query that
  * reaches it stops expanding, still reranks, and makes the search return
  * DVS_ERR_HOP_LIMIT. */
@@ -175,6 +183,11 @@ dvs_status dvs_kernel_times(dvs_index* index, uint32_t slot, uint32_t* searches,
  * d_factor[q] = {add, k1xSumq, kBxSumq} (RabitqQueryFactor, 12 bytes). */
 dvs_status dvs_query_prepare(const float* d_query, const float* d_P, const float* d_centroid, float* d_rot_query,
                              float* d_factor, uint32_t nq, uint32_t dim, uint32_t bits, void* stream);
+
+/* dvs_query_prepare with the rotation on tcgen05 tensor cores (3xTF32).
+ * Returns DVS_ERR_TIMEOUT if a bounded wait inside the kernel expired. */
+dvs_status dvs_query_prepare_tc(const float* d_query, const float* d_P, const float* d_centroid, float* d_rot_query,
+                                float* d_factor, uint32_t nq, uint32_t dim, uint32_t bits, void* stream);
 
 /* gpu::launch_batch_rabitq_distances (src/gpu/gpu_kernel_launcher.hh:53-59):
  * n records of rabitq_size bytes each, packed back to back as the reference

@@ -89,3 +89,29 @@ def test_kernel_entry_points_reject_bad_arguments(gpu):
     assert L.dvs_rabitq_estimate(one, one, one, one, 4, 8, 3, None) == 5  # DVS_ERR_BITS
     assert L.dvs_l2_distances(one, one, one, 4, 0, None) == 4             # DVS_ERR_DIM
     assert L.dvs_l2_distances(one, one, one, 0, 8, None) == 0             # empty batch: no launch
+
+
+@pytest.mark.parametrize("dim,nq", [(96, 300), (128, 129), (30, 5), (200, 64), (960, 130)])
+def test_query_prepare_tensor_cores_accuracy(gpu, oracle, dim, nq):
+    """tcgen05 3xTF32 rotation: within 1e-5 of the row's largest |q'| of the fp64
+    product (fp32-level accuracy); factors equal the reference arithmetic applied
+    to its rotated rows, bit for bit."""
+    import torch
+
+    from dvstor_b200._lib import check, lib, ptr
+
+    P = oracle.rotation_matrix(dim, 13)
+    c_rot = np.random.default_rng(4).standard_normal(dim).astype(np.float32)
+    Q = np.random.default_rng(dim).standard_normal((nq, dim)).astype(np.float32)
+    dQ, dP, dc = _dev(Q), _dev(P), _dev(c_rot)
+    qr = torch.empty((nq, dim), dtype=torch.float32, device="cuda")
+    fac = torch.empty((nq, 3), dtype=torch.float32, device="cuda")
+    check(lib().dvs_query_prepare_tc(ptr(dQ), ptr(dP), ptr(dc), ptr(qr), ptr(fac), nq, dim, 4, None))
+    _sync()
+    got = qr.cpu().numpy()
+    ref = Q.astype(np.float64) @ P.reshape(dim, dim).astype(np.float64).T  # row j of P.reshape = column j of P
+    scale = np.abs(ref).max(axis=1, keepdims=True)
+    assert (np.abs(got - ref) / scale).max() < 1e-5
+    f = fac.cpu().numpy()
+    for i in range(0, nq, max(1, nq // 7)):
+        np.testing.assert_array_equal(f[i].view(np.uint32), oracle.query_factors(got[i], c_rot, 4).view(np.uint32))

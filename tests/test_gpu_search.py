@@ -32,6 +32,8 @@ def cases(oracle, tmp_path_factory):
         "ip": Case(oracle, tmp, "ip", normalized_gaussian(2000, 48, 8), 16, 32, metric="ip"),
         "shards": Case(oracle, tmp, "shards", uniform_int_data(3000, 32, 9), 24, 48, M=3),
         "tiny": Case(oracle, tmp, "tiny", normalized_gaussian(12, 8, 10), 4, 8),
+        "d160": Case(oracle, tmp, "d160", normalized_gaussian(1500, 160, 11), 24, 32),
+        "d256r48": Case(oracle, tmp, "d256r48", normalized_gaussian(1200, 256, 12), 48, 48),
     }
 
 
@@ -45,7 +47,8 @@ def run_both(gpu, oracle, case, Q, k, L, mode="rabitq_gpu"):
 
 
 @pytest.mark.parametrize("name,L", [("int128", 64), ("gauss96", 64), ("gauss96", 128), ("r48", 100), ("bits2", 32),
-                                    ("bits1", 48), ("ragged", 40), ("ip", 32), ("shards", 64)])
+                                    ("bits1", 48), ("ragged", 40), ("ip", 32), ("shards", 64), ("d160", 40),
+                                    ("d256r48", 48)])
 @pytest.mark.parametrize("mode", ["rabitq_gpu", "exact_gpu"])
 def test_search_matches_oracle(gpu, oracle, cases, name, L, mode):
     case = cases[name]
@@ -233,3 +236,30 @@ def test_sharded_rejects_bad_device_counts(gpu, cases):
     with pytest.raises(gpu.DvsError) as e:
         gpu.Index(cases["gauss96"].prefix, devices=(0, 0, 0), placement="shard")
     assert e.value.name == "DVS_ERR_ARG"
+
+
+@pytest.mark.parametrize("name,L", [("gauss96", 64), ("d256r48", 48)])
+def test_tensor_core_rotation_search(gpu, oracle, cases, name, L):
+    """With the rotation on tensor cores the rest of the path is unchanged: the
+    search equals the oracle's knn fed the GPU's rotated queries and factors."""
+    import torch
+
+    from dvstor_b200._lib import check, lib, ptr
+
+    case = cases[name]
+    d = case.idx.dim
+    Q = normalized_gaussian(300, d, 61)
+    dQ = torch.from_numpy(Q).cuda()
+    dP = torch.from_numpy(case.idx.P).cuda()
+    dc = torch.from_numpy(case.idx.c_rot).cuda()
+    qr = torch.empty((300, d), dtype=torch.float32, device="cuda")
+    fac = torch.empty((300, 3), dtype=torch.float32, device="cuda")
+    check(lib().dvs_query_prepare_tc(ptr(dQ), ptr(dP), ptr(dc), ptr(qr), ptr(fac), 300, d, case.idx.bits, None))
+    torch.cuda.synchronize()
+    with gpu.Index(case.prefix) as ix:
+        ix.set_rotation("tensor")
+        ids, dist, st = ix.search(Q, 10, L, stats=True)
+    o_ids, o_d, o_cnt, b_ids, b_d = case.idx.knn(Q, 10, L, q_rot=qr.cpu().numpy(), factors=fac.cpu().numpy(),
+                                                 beam_cap=L + 64)
+    assert_results_match(ids, dist, o_ids, o_d, b_ids, b_d)
+    assert st["estimates"] == int(o_cnt[:, 1].sum())
