@@ -201,39 +201,6 @@ __global__ void __launch_bounds__(128, 1) rotate_tc_kernel(const float* __restri
   }
 }
 
-// Factors of rabitq_query_prepare_kernel<4,B> from rotated rows (one quad per query).
-__global__ void factors_kernel(const float* __restrict__ qrot, uint32_t qrot_stride, const float* __restrict__ c,
-                               float* __restrict__ qfac, uint32_t fac_stride, uint32_t dim, uint32_t nq, float c_b) {
-  const uint32_t gq = (blockIdx.x * blockDim.x + threadIdx.x) >> 2;
-  const uint32_t t = threadIdx.x & 3;
-  float sq = 0.f, sm = 0.f;
-  if (gq < nq) {
-    const float* r = qrot + size_t(gq) * qrot_stride;
-    for (uint32_t j = t; j < dim; j += 4) {
-      const float v = r[j];
-      const float diff = __fsub_rn(v, __ldg(c + j));
-      sq = __fmaf_rn(diff, diff, sq);
-      sm = __fadd_rn(sm, v);
-    }
-  }
-  sq = quad_butterfly(sq);
-  sm = quad_butterfly(sm);
-  if (gq < nq && t == 0) {
-    float* f = qfac + size_t(gq) * fac_stride;
-    f[0] = sq;
-    f[1] = __fmul_rn(-0.5f, sm);
-    f[2] = __fmul_rn(c_b, sm);
-    if (fac_stride > 3) f[3] = 0.f;
-  }
-}
-
-__global__ void zero_pad_kernel(float* __restrict__ qrot, uint32_t stride, uint32_t dim, uint32_t nq) {
-  const uint32_t pad = stride - dim;
-  const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= uint64_t(nq) * pad) return;
-  qrot[(i / pad) * stride + dim + i % pad] = 0.f;
-}
-
 }  // namespace
 
 uint32_t rotate_tc_tile_n(uint32_t dim) {
@@ -260,13 +227,7 @@ cudaError_t launch_prepare_tc(const float* queries, uint32_t q_stride, const flo
   rotate_tc_kernel<<<grid, 128, smem, stream>>>(queries, q_stride, P, qrot, qrot_stride, dim, nq, nt, err);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (qrot_stride > dim) {
-    const uint64_t tot = uint64_t(nq) * (qrot_stride - dim);
-    zero_pad_kernel<<<uint32_t((tot + 255) / 256), 256, 0, stream>>>(qrot, qrot_stride, dim, nq);
-  }
-  const float c_b = -static_cast<float>((1u << bits) - 1u) / 2.0f;
-  factors_kernel<<<(nq * 4 + 127) / 128, 128, 0, stream>>>(qrot, qrot_stride, c_rot, qfac, fac_stride, dim, nq, c_b);
-  return cudaGetLastError();
+  return launch_query_factors(qrot, qrot_stride, c_rot, qfac, fac_stride, dim, bits, nq, stream);
 }
 
 }  // namespace dvs

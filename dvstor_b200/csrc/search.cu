@@ -590,129 +590,6 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
   }
 }
 
-// q' = P^T q in a fixed order (sequential fmaf over i) and the factors of
-// rabitq_query_prepare_kernel<4,B> (src/gpu/kernels/distance_kernels.cuh:470-501).
-__global__ void __launch_bounds__(128) prepare_kernel(const float* __restrict__ Q, uint32_t q_stride,
-                                                      const float* __restrict__ P, const float* __restrict__ c,
-                                                      float* __restrict__ qrot, uint32_t qrot_stride,
-                                                      float* __restrict__ qfac, uint32_t fac_stride, uint32_t dim,
-                                                      uint32_t nq, float c_b) {
-  extern __shared__ float sh[];
-  float* qs = sh;
-  float* rs = sh + dim;
-  for (uint32_t q = blockIdx.x; q < nq; q += gridDim.x) {
-    for (uint32_t j = threadIdx.x; j < dim; j += blockDim.x) qs[j] = Q[size_t(q) * q_stride + j];
-    __syncthreads();
-    for (uint32_t j = threadIdx.x; j < dim; j += blockDim.x) {
-      const float* col = P + size_t(j) * dim;
-      float acc = 0.f;
-      for (uint32_t i = 0; i < dim; ++i) acc = __fmaf_rn(__ldg(col + i), qs[i], acc);
-      rs[j] = acc;
-      qrot[size_t(q) * qrot_stride + j] = acc;
-    }
-    for (uint32_t j = dim + threadIdx.x; j < qrot_stride; j += blockDim.x) qrot[size_t(q) * qrot_stride + j] = 0.f;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      const uint32_t lane = threadIdx.x;
-      float sq = 0.f, sm = 0.f;
-      if (lane < 4) {
-        for (uint32_t j = lane; j < dim; j += 4) {
-          const float diff = __fsub_rn(rs[j], __ldg(c + j));
-          sq = __fmaf_rn(diff, diff, sq);
-          sm = __fadd_rn(sm, rs[j]);
-        }
-      }
-      sq = quad_butterfly(sq);
-      sm = quad_butterfly(sm);
-      if (lane == 0) {
-        qfac[size_t(q) * fac_stride + 0] = sq;
-        qfac[size_t(q) * fac_stride + 1] = __fmul_rn(-0.5f, sm);
-        qfac[size_t(q) * fac_stride + 2] = __fmul_rn(c_b, sm);
-        if (fac_stride > 3) qfac[size_t(q) * fac_stride + 3] = 0.f;
-      }
-    }
-    __syncthreads();
-  }
-}
-
-// The same prepare for dim <= 128 with P^T and a tile of 64 queries staged in
-// shared memory; each thread owns one output column for 8 queries, so every
-// P^T element loaded feeds 8 FMAs.  Each output is still the sequential fmaf
-// chain over i, so results equal prepare_kernel's bit for bit.
-constexpr uint32_t kPrepTileQ = 64;
-
-__global__ void __launch_bounds__(256) prepare_tile_kernel(const float* __restrict__ Q, uint32_t q_stride,
-                                                           const float* __restrict__ P, const float* __restrict__ c,
-                                                           float* __restrict__ qrot, uint32_t qrot_stride,
-                                                           float* __restrict__ qfac, uint32_t fac_stride,
-                                                           uint32_t dim, uint32_t nq, float c_b) {
-  extern __shared__ __align__(16) float sm[];
-  float* PT = sm;                        // dim x dim, PT[i*dim + j] = P[j*dim + i]
-  float* qT = PT + dim * dim;            // dim x 64, qT[i*64 + b]
-  float* rs = qT + dim * kPrepTileQ;     // 64 x dim rotated queries
-  for (uint32_t t = threadIdx.x; t < dim * dim; t += blockDim.x) {
-    const uint32_t j = t / dim, i = t - j * dim;
-    PT[i * dim + j] = P[t];
-  }
-  for (uint32_t q0 = blockIdx.x * kPrepTileQ; q0 < nq; q0 += gridDim.x * kPrepTileQ) {
-    const uint32_t nb = min(kPrepTileQ, nq - q0);
-    for (uint32_t t = threadIdx.x; t < dim * kPrepTileQ; t += blockDim.x) {
-      const uint32_t b = t / dim, i = t - b * dim;
-      qT[i * kPrepTileQ + b] = b < nb ? Q[size_t(q0 + b) * q_stride + i] : 0.f;
-    }
-    __syncthreads();
-    const uint32_t tiles = dim * (kPrepTileQ / 8);
-    for (uint32_t t = threadIdx.x; t < tiles; t += blockDim.x) {
-      const uint32_t j = t % dim, bg = t / dim;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (uint32_t i = 0; i < dim; ++i) {
-        const float p = PT[i * dim + j];
-        const float4 qa = *reinterpret_cast<const float4*>(qT + i * kPrepTileQ + 8 * bg);
-        const float4 qb = *reinterpret_cast<const float4*>(qT + i * kPrepTileQ + 8 * bg + 4);
-        acc[0] = __fmaf_rn(p, qa.x, acc[0]);
-        acc[1] = __fmaf_rn(p, qa.y, acc[1]);
-        acc[2] = __fmaf_rn(p, qa.z, acc[2]);
-        acc[3] = __fmaf_rn(p, qa.w, acc[3]);
-        acc[4] = __fmaf_rn(p, qb.x, acc[4]);
-        acc[5] = __fmaf_rn(p, qb.y, acc[5]);
-        acc[6] = __fmaf_rn(p, qb.z, acc[6]);
-        acc[7] = __fmaf_rn(p, qb.w, acc[7]);
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) rs[(8 * bg + k) * dim + j] = acc[k];
-    }
-    __syncthreads();
-    for (uint32_t t = threadIdx.x; t < nb * qrot_stride; t += blockDim.x) {
-      const uint32_t b = t / qrot_stride, j = t - b * qrot_stride;
-      qrot[size_t(q0 + b) * qrot_stride + j] = j < dim ? rs[b * dim + j] : 0.f;
-    }
-    // factors: one lane quad per query, the 4-lane butterfly of rabitq_query_prepare_kernel
-    const uint32_t lane = threadIdx.x & 31, quad = threadIdx.x >> 2;
-    for (uint32_t b0 = 0; b0 < kPrepTileQ; b0 += blockDim.x / 4) {
-      const uint32_t b = b0 + quad;
-      float sq = 0.f, sm2 = 0.f;
-      if (b < nb) {
-        for (uint32_t j = lane & 3; j < dim; j += 4) {
-          const float v = rs[b * dim + j];
-          const float diff = __fsub_rn(v, __ldg(c + j));
-          sq = __fmaf_rn(diff, diff, sq);
-          sm2 = __fadd_rn(sm2, v);
-        }
-      }
-      sq = quad_butterfly(sq);
-      sm2 = quad_butterfly(sm2);
-      if (b < nb && (lane & 3) == 0) {
-        float* f = qfac + size_t(q0 + b) * fac_stride;
-        f[0] = sq;
-        f[1] = __fmul_rn(-0.5f, sm2);
-        f[2] = __fmul_rn(c_b, sm2);
-        if (fac_stride > 3) f[3] = 0.f;
-      }
-    }
-    __syncthreads();
-  }
-}
-
 // batch_rabitq_distance_kernel on the reference's staged layout (records back
 // to back, rabitq_size bytes each, factors possibly unaligned): one thread per
 // record, byte-wise reads, same chain order.
@@ -803,30 +680,6 @@ void launch_rch(int rch, const SearchArgs& a, dim3 g, dim3 b, size_t smem, cudaS
 }
 
 }  // namespace
-
-cudaError_t launch_prepare(const float* queries, uint32_t q_stride, const float* P, const float* c_rot, float* qrot,
-                           uint32_t qrot_stride, float* qfac, uint32_t fac_stride, uint32_t dim, uint32_t bits,
-                           uint32_t nq, cudaStream_t stream) {
-  if (nq == 0) return cudaSuccess;
-  const float c_b = -static_cast<float>((1u << bits) - 1u) / 2.0f;
-  if (dim <= 128) {
-    const size_t smem = (size_t(dim) * dim + size_t(dim) * kPrepTileQ * 2) * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(prepare_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const uint32_t tiles = (nq + kPrepTileQ - 1) / kPrepTileQ;
-    const uint32_t grid = tiles < uint32_t(2 * sms) ? tiles : uint32_t(2 * sms);
-    prepare_tile_kernel<<<grid, 256, smem, stream>>>(queries, q_stride, P, c_rot, qrot, qrot_stride, qfac, fac_stride,
-                                                     dim, nq, c_b);
-    return cudaGetLastError();
-  }
-  const uint32_t grid = nq < 65535u ? nq : 65535u;
-  prepare_kernel<<<grid, 128, 2 * dim * sizeof(float), stream>>>(queries, q_stride, P, c_rot, qrot, qrot_stride,
-                                                                  qfac, fac_stride, dim, nq, c_b);
-  return cudaGetLastError();
-}
 
 cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, uint32_t wpb, size_t smem, int* bps) {
   const bool two = R > 32;

@@ -92,9 +92,15 @@ __host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t
   return 4 * cap_pad + 2 * dim_pad + 256 + hcap;
 }
 
+// q' = P^T q (the sequential fmaf chain over i per output) and the query
+// factors, for nq queries; rows padded with zeros to qrot_stride.
 cudaError_t launch_prepare(const float* queries, uint32_t q_stride, const float* P, const float* c_rot, float* qrot,
                            uint32_t qrot_stride, float* qfac, uint32_t fac_stride, uint32_t dim, uint32_t bits,
                            uint32_t nq, cudaStream_t stream);
+
+// The factors alone, from rows already rotated in qrot (and their zero padding).
+cudaError_t launch_query_factors(float* qrot, uint32_t qrot_stride, const float* c_rot, float* qfac,
+                                 uint32_t fac_stride, uint32_t dim, uint32_t bits, uint32_t nq, cudaStream_t stream);
 
 // Q' = Q P^T on tcgen05 tensor cores (3xTF32) plus the query factors; a
 // bounded mbarrier wait that expires ORs kErrTimeout into *err.

@@ -60,13 +60,15 @@ def test_rabitq_estimate_bit_exact(gpu, oracle, bits, dim):
     np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("dim,bits", [(96, 4), (128, 4), (30, 2), (960, 4)])
-def test_query_prepare_bit_exact(gpu, oracle, dim, bits):
+@pytest.mark.parametrize("dim,bits,nq", [(96, 4, 37), (128, 4, 130), (30, 2, 37), (960, 4, 37), (960, 4, 130),
+                                         (131, 4, 65), (200, 1, 64), (257, 4, 3)])
+def test_query_prepare_bit_exact(gpu, oracle, dim, bits, nq):
+    """Two kernels: P^T resident in shared memory (dim <= 128) and the
+    register-tiled product (dim > 128); tile edges in both query and output."""
     import torch
 
     from dvstor_b200._lib import check, lib, ptr
 
-    nq = 37
     P = oracle.rotation_matrix(dim, 11)
     c_rot = np.random.default_rng(3).standard_normal(dim).astype(np.float32)
     Q = normalized_gaussian(nq, dim, 2)

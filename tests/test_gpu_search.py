@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 from conftest import assert_results_match, normalized_gaussian, uniform_int_data, write_oracle_index
+from dvstor_b200.datasets import low_rank_uniform
 
 pytestmark = pytest.mark.gpu
 
@@ -34,6 +35,8 @@ def cases(oracle, tmp_path_factory):
         "tiny": Case(oracle, tmp, "tiny", normalized_gaussian(12, 8, 10), 4, 8),
         "d160": Case(oracle, tmp, "d160", normalized_gaussian(1500, 160, 11), 24, 32),
         "d256r48": Case(oracle, tmp, "d256r48", normalized_gaussian(1200, 256, 12), 48, 48),
+        # the 1M x 960 workload's shape at small n: low-rank uniform data, R=48
+        "d960r48": Case(oracle, tmp, "d960r48", low_rank_uniform(2500, 960, 4), 48, 64),
     }
 
 
@@ -48,16 +51,32 @@ def run_both(gpu, oracle, case, Q, k, L, mode="rabitq_gpu"):
 
 @pytest.mark.parametrize("name,L", [("int128", 64), ("gauss96", 64), ("gauss96", 128), ("r48", 100), ("bits2", 32),
                                     ("bits1", 48), ("ragged", 40), ("ip", 32), ("shards", 64), ("d160", 40),
-                                    ("d256r48", 48)])
+                                    ("d256r48", 48), ("d960r48", 200)])
 @pytest.mark.parametrize("mode", ["rabitq_gpu", "exact_gpu"])
 def test_search_matches_oracle(gpu, oracle, cases, name, L, mode):
     case = cases[name]
     d = case.idx.dim
-    Q = (uniform_int_data(300, d, 99) if name in ("int128", "shards") else normalized_gaussian(300, d, 99))
+    if name in ("int128", "shards"):
+        Q = uniform_int_data(300, d, 99)
+    elif name == "d960r48":
+        Q = low_rank_uniform(300, d, 99)
+    else:
+        Q = normalized_gaussian(300, d, 99)
     k = 10
     ids, dist, st, o_ids, o_d, o_cnt, b_ids, b_d = run_both(gpu, oracle, case, Q, k, L, mode)
     assert_results_match(ids, dist, o_ids, o_d, b_ids, b_d)
     assert st["expansions"] == int(o_cnt[:, 0].sum())
+    assert st["estimates"] == int(o_cnt[:, 1].sum())
+    assert st["reranked"] == int(o_cnt[:, 2].sum())
+
+
+@pytest.mark.parametrize("mode", ["rabitq_gpu", "exact_gpu"])
+def test_k100_wide_records(gpu, oracle, cases, mode):
+    """k = 100 at beam width 200 on D = 960, R = 48 (488-byte codes)."""
+    case = cases["d960r48"]
+    Q = low_rank_uniform(120, 960, 98)
+    ids, d, st, o_ids, o_d, o_cnt, b_ids, b_d = run_both(gpu, oracle, case, Q, 100, 200, mode)
+    assert_results_match(ids, d, o_ids, o_d, b_ids, b_d)
     assert st["estimates"] == int(o_cnt[:, 1].sum())
     assert st["reranked"] == int(o_cnt[:, 2].sum())
 
