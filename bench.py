@@ -50,6 +50,7 @@ def parse_args():
     ap.add_argument("--beam-width", type=int, default=None)
     ap.add_argument("--k", type=int, default=10)
     ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--n", type=int, default=None, help="index size override (reduced-size runs of a workload)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--cache", default=os.environ.get("DVS_BENCH_CACHE", "/tmp/dvs_b200_bench"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -95,15 +96,15 @@ class Dist:
             self.pg.destroy_process_group()
 
 
-def workload_params(name):
+def workload_params(name, n=None):
     from dvstor_b200 import datasets
 
-    gen, n, dim, seed, R, build_L, search_L, k = datasets.WORKLOADS[name]
-    return dict(gen=gen, n=n, dim=dim, seed=seed, R=R, build_L=build_L, search_L=search_L, k=k)
+    gen, n0, dim, seed, R, build_L, search_L, k = datasets.WORKLOADS[name]
+    return dict(gen=gen, n=n or n0, dim=dim, seed=seed, R=R, build_L=build_L, search_L=search_L, k=k)
 
 
 def index_prefix(args, wp):
-    tag = f"{args.workload}_R{wp['R']}_L{wp['build_L']}_b4_s1234"
+    tag = f"{args.workload}_n{wp['n']}_R{wp['R']}_L{wp['build_L']}_b4_s1234"
     return os.path.join(args.cache, tag, "idx")
 
 
@@ -203,6 +204,13 @@ def recall(ids, gt):
     return float(np.mean([len(set(ids[i][:k].tolist()) & set(gt[i].tolist())) / k for i in range(len(gt))]))
 
 
+def index_device_bytes(info):
+    """HBM bytes of one replica: adjacency, records (16-byte padded), vectors, ids."""
+    rec = (((info.rabitq_bits * info.dim + 7) // 8 + 3) // 4 * 4 + 8 + 15) // 16 * 16
+    vec = (info.dim + 3) // 4 * 16
+    return info.num_vectors * (4 * info.R + rec + vec + 4)
+
+
 def bytes_per_query(dim, R, bits, k, H, E, Cr, nq):
     """Algorithmic bytes of one query: query row, H adjacency rows (R ids + count),
     E RaBitQ records (codes + add + rescale), C_r rerank rows, the rotation
@@ -257,7 +265,7 @@ def run_reference(args):
     from dvstor_b200 import datasets
     from oracle import oracle as O
 
-    wp = workload_params(args.workload)
+    wp = workload_params(args.workload, args.n)
     L = args.beam_width or wp["search_L"]
     dist_single = Dist.__new__(Dist)
     dist_single.world, dist_single.rank, dist_single.local, dist_single.pg = 1, 0, 0, None
@@ -306,7 +314,7 @@ def run_ours(args):
     import dvstor_b200 as D
     from dvstor_b200 import datasets
 
-    wp = workload_params(args.workload)
+    wp = workload_params(args.workload, args.n)
     L = args.beam_width or wp["search_L"]
     k = args.k
     B = args.batch
@@ -405,7 +413,8 @@ def run_ours(args):
             "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"],
                        "build_L": wp["build_L"], "rabitq_bits": 4, "k": k, "beam_width": L,
                        "queries_per_step_per_gpu": B, "parallelism": f"replicas x{dist.world}",
-                       "l2": "index 0.58 GB larger than L2, not flushed; fresh query batch every step"},
+                       "l2": f"index {index_device_bytes(info) / 1e9:.2f} GB larger than L2, not flushed; "
+                             "fresh query batch every step"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": tr, "peak_source": f"{peak_kind} hbm_gbs",
                          "kernel": "search_kernel", "kernel_ms": search_avg_ms,

@@ -293,9 +293,6 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
                      uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st, bool timed) {
   const DevLayout& lay = d.lay;
   const bool rabitq = mode == DVS_MODE_RABITQ_GPU;
-  if (rabitq && lay.bits != 1 && lay.bits != 2 && lay.bits != 4)
-    return fail(DVS_ERR_BITS, "rabitq_gpu search supports 1-, 2- and 4-bit codes on the device; index has " +
-                                  std::to_string(lay.bits));
   if (lay.R > 64) return fail(DVS_ERR_UNSUPPORTED, "max out-degree above 64 is not supported by the search kernel");
   const uint32_t cap = rabitq ? L + kBeamSlack : L;
   LaunchShape s;
@@ -670,8 +667,8 @@ dvs_status dvs_query_prepare_tc(const float* d_query, const float* d_P, const fl
 dvs_status dvs_rabitq_estimate(const float* d_rot_query, const float* d_factor, const uint8_t* d_records,
                                float* d_dist, uint32_t n, uint32_t dim, uint32_t bits, void* stream) {
   if (!d_rot_query || !d_factor || !d_records || !d_dist) return fail(DVS_ERR_ARG, "null buffer");
-  if (bits != 1 && bits != 2 && bits != 4)
-    return fail(DVS_ERR_BITS, "the estimator supports 1-, 2- and 4-bit codes; got " + std::to_string(bits));
+  if (bits != 1 && bits != 2 && bits != 4 && bits != 8)
+    return fail(DVS_ERR_BITS, "bits must be 1, 2, 4, or 8; got " + std::to_string(bits));
   DVS_CUDA(dvs::launch_estimate_ref_layout(d_rot_query, d_factor, d_records, d_dist, n, dim, bits,
                                            static_cast<cudaStream_t>(stream)));
   return DVS_OK;

@@ -139,6 +139,21 @@ __device__ __forceinline__ void rabitq_word(uint32_t word, const float* __restri
   }
 }
 
+// One char4 step of batch_rabitq_8bit_distance_kernel
+// (src/gpu/kernels/distance_kernels.cuh:181-221): bytes b0..b3 of `word` are
+// dims 4i..4i+3; x0*q0 + x1*q1 + x2*q2 + x3*q3 as nvcc contracts it
+// (fma(x3,q3, fma(x2,q2, fma(x0,q0, x1*q1)))), to be added to chain i mod 4.
+__device__ __forceinline__ float rabitq_char4(uint32_t word, float4 q) {
+  const float x0 = __fsub_rn(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7440u)), 8388608.0f);
+  const float x1 = __fsub_rn(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7441u)), 8388608.0f);
+  const float x2 = __fsub_rn(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7442u)), 8388608.0f);
+  const float x3 = __fsub_rn(__uint_as_float(__byte_perm(word, 0x4B000000u, 0x7443u)), 8388608.0f);
+  float t = __fmul_rn(x1, q.y);
+  t = __fmaf_rn(x0, q.x, t);
+  t = __fmaf_rn(x2, q.z, t);
+  return __fmaf_rn(x3, q.w, t);
+}
+
 // Medoid seed distance (L2Distance / IPDistance on the host in the reference,
 // src/common/distance.hh:80-159): eight AVX lanes over 16-float chunks, a
 // left-to-right horizontal sum, then the tail.  Lanes 0..7 of the warp each own

@@ -79,8 +79,6 @@ extern "C" dvs_status dvs_search_device_noalloc(dvs_index* index, uint32_t devic
   if (!d_queries || !d_out_ids || !d_out_dist) return fail(DVS_ERR_ARG, "null buffer");
   const bool rabitq = mode == DVS_MODE_RABITQ_GPU;
   const DevLayout& lay = v.lay;
-  if (rabitq && lay.bits != 1 && lay.bits != 2 && lay.bits != 4)
-    return fail(DVS_ERR_BITS, "rabitq_gpu search supports 1-, 2- and 4-bit codes on the device");
   if (lay.R > 64) return fail(DVS_ERR_UNSUPPORTED, "max out-degree above 64 is not supported by the search kernel");
   const size_t per_query = size_t(lay.vec_stride) * 4 + 16;
   const size_t max_nq = kNoAllocQueryBytes / per_query;

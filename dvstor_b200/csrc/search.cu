@@ -181,37 +181,87 @@ __device__ __forceinline__ uint32_t visit16(uint32_t* tab, uint32_t nb, float in
   return kNoRoom;
 }
 
-// RaBitQ estimate of one record by one lane (all four chains on this lane).
+// One 32-bit word of codes into the chains.  B in {1,2,4}: dim j -> chain
+// j & 3 (rabitq_word).  B = 8: the word is one char4 step of the 8-bit kernel
+// and goes whole to chain (word index) & 3 = e, the word's position in its
+// 16-byte chunk; words past floor(dim/4) are not part of the sum.
 template <int BITS>
-__device__ __forceinline__ float estimate_lane(const DevLayout& ix, uint32_t c, const float* __restrict__ qr,
-                                               float q_add, float q_k1) {
-  constexpr int kPer = 32 / BITS;
-  const uint4* r = reinterpret_cast<const uint4*>(rec_row(ix, c));
-  const uint32_t nch = (ix.code_words + 2 + 3) >> 2;
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, add_o = 0.f, rs_o = 0.f;
-  for (uint32_t c0 = 0; c0 < nch; c0 += 8) {
-    uint4 v[8];
+__device__ __forceinline__ void code_word(uint32_t word, uint32_t wi, int e, const DevLayout& ix,
+                                          const float* __restrict__ qr, float& s0, float& s1, float& s2, float& s3) {
+  if constexpr (BITS == 8) {
+    if (wi < (ix.dim >> 2)) {
+      const float t = rabitq_char4(word, *reinterpret_cast<const float4*>(qr + 4 * wi));
+      switch (e) {
+        case 0: s0 = __fadd_rn(s0, t); break;
+        case 1: s1 = __fadd_rn(s1, t); break;
+        case 2: s2 = __fadd_rn(s2, t); break;
+        default: s3 = __fadd_rn(s3, t); break;
+      }
+    }
+  } else {
+    rabitq_word<BITS>(word, qr, wi * (32 / BITS), ix.dim, s0, s1, s2, s3);
+  }
+}
+
+// Chain t of one record's estimate, computed by lane t of a lane quad: the
+// reference kernel's own tile-of-4 split (lane t sums dims j = t mod 4 for
+// B in {1,2,4}, char4 steps c = t mod 4 for B = 8), in ascending order.  Used
+// for records wider than 128 bytes, where one lane per record would leave
+// lanes idle and unroll too much code.  Lane 0 also returns the record's add
+// and rescale factors.
+template <int BITS>
+__device__ __forceinline__ float estimate_quad_chain(const DevLayout& ix, uint32_t c, const float* __restrict__ qr,
+                                                     uint32_t t, float& add_o, float& rs_o) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(rec_row(ix, c));
+  if (t == 0) {
+    add_o = __uint_as_float(__ldg(r + ix.code_words));
+    rs_o = __uint_as_float(__ldg(r + ix.code_words + 1));
+  }
+  float s = 0.f;
+  if constexpr (BITS == 8) {
+    const uint32_t nw = ix.dim >> 2;
+    uint32_t w = t;
+    for (; w + 12 < nw; w += 16) {
+      const uint32_t a0 = __ldg(r + w), a1 = __ldg(r + w + 4), a2 = __ldg(r + w + 8), a3 = __ldg(r + w + 12);
+      s = __fadd_rn(s, rabitq_char4(a0, *reinterpret_cast<const float4*>(qr + 4 * w)));
+      s = __fadd_rn(s, rabitq_char4(a1, *reinterpret_cast<const float4*>(qr + 4 * (w + 4))));
+      s = __fadd_rn(s, rabitq_char4(a2, *reinterpret_cast<const float4*>(qr + 4 * (w + 8))));
+      s = __fadd_rn(s, rabitq_char4(a3, *reinterpret_cast<const float4*>(qr + 4 * (w + 12))));
+    }
+    for (; w < nw; w += 4) s = __fadd_rn(s, rabitq_char4(__ldg(r + w), *reinterpret_cast<const float4*>(qr + 4 * w)));
+  } else {
+    constexpr uint32_t kPer = 32 / BITS, kMask = (1u << BITS) - 1u;
+    const uint4* r4 = reinterpret_cast<const uint4*>(r);
+    const uint32_t nch = (ix.dim / kPer) >> 2;  // 16-byte chunks whose every dim is < dim
+    const uint32_t sh0 = BITS * t;
+    for (uint32_t ch = 0; ch < nch; ch += 4) {
+      uint4 v[4];
 #pragma unroll
-    for (int t = 0; t < 8; ++t)
-      if (c0 + t < nch) v[t] = __ldg(r + c0 + t);
+      for (int k = 0; k < 4; ++k)
+        if (ch + k < nch) v[k] = __ldg(r4 + ch + k);
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      if (c0 + t < nch) {
-        const uint32_t w[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+      for (int k = 0; k < 4; ++k) {
+        if (ch + k < nch) {
+          const uint32_t wv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t wi = (c0 + t) * 4 + e;
-          if (wi < ix.code_words)
-            rabitq_word<BITS>(w[e], qr, wi * kPer, ix.dim, s0, s1, s2, s3);
-          else if (wi == ix.code_words)
-            add_o = __uint_as_float(w[e]);
-          else if (wi == ix.code_words + 1)
-            rs_o = __uint_as_float(w[e]);
+          for (int e = 0; e < 4; ++e) {
+            const float* q = qr + ((ch + k) * 4 + e) * kPer + t;
+#pragma unroll
+            for (uint32_t i = 0; i < kPer / 4; ++i)
+              s = __fmaf_rn(small_u2f((wv[e] >> (sh0 + 4 * BITS * i)) & kMask), q[4 * i], s);
+          }
         }
       }
     }
+    // words past the last whole chunk, the partial last word included
+    for (uint32_t wi = nch * 4; wi * kPer < ix.dim; ++wi) {
+      const uint32_t word = __ldg(r + wi);
+      const uint32_t j0 = wi * kPer;
+      for (uint32_t n = t; n < kPer && j0 + n < ix.dim; n += 4)
+        s = __fmaf_rn(small_u2f((word >> (BITS * n)) & kMask), qr[j0 + n], s);
+    }
   }
-  return rabitq_finish(tile4_sum(s0, s1, s2, s3), add_o, rs_o, q_add, q_k1, float((1u << BITS) - 1u));
+  return s;
 }
 
 // Exact L2 of `count` rows (slot ids in `rows`) against q, written to `out`;
@@ -236,7 +286,6 @@ __device__ __forceinline__ void l2_rows_warp(const DevLayout& ix, const float* _
 template <int BITS, int RCH>
 __device__ __forceinline__ float estimate_regs(const uint4 (&v)[RCH], const DevLayout& ix, const float* __restrict__ qr,
                                                float q_add, float q_k1) {
-  constexpr int kPer = 32 / BITS;
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, add_o = 0.f, rs_o = 0.f;
 #pragma unroll
   for (int t = 0; t < RCH; ++t) {
@@ -245,7 +294,7 @@ __device__ __forceinline__ float estimate_regs(const uint4 (&v)[RCH], const DevL
     for (int e = 0; e < 4; ++e) {
       const uint32_t wi = t * 4 + e;
       if (wi < ix.code_words)
-        rabitq_word<BITS>(w[e], qr, wi * kPer, ix.dim, s0, s1, s2, s3);
+        code_word<BITS>(w[e], wi, e, ix, qr, s0, s1, s2, s3);
       else if (wi == ix.code_words)
         add_o = __uint_as_float(w[e]);
       else if (wi == ix.code_words + 1)
@@ -465,7 +514,15 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
       if (!rabitq) {
         l2_rows_warp(ix, qv, cid, m, cd, lane, 0xFFFFFFFFu);
       } else if (RCH == 0) {
-        for (uint32_t i = lane; i < m; i += 32) cd[i] = estimate_lane<BITS>(ix, cid[i], qr, q_add, q_k1);
+        // wide records: 8 per round, a lane quad each, chains reduced with the tile butterfly
+        const uint32_t t = lane & 3;
+        for (uint32_t i0 = 0; i0 < m; i0 += 8) {
+          const uint32_t i = i0 + (lane >> 2);
+          float part = 0.f, add_o = 0.f, rs_o = 0.f;
+          if (i < m) part = estimate_quad_chain<BITS>(ix, cid[i], qr, t, add_o, rs_o);
+          const float dot = quad_butterfly(part);
+          if (i < m && t == 0) cd[i] = rabitq_finish(dot, add_o, rs_o, q_add, q_k1, float((1u << BITS) - 1u));
+        }
       }
       __syncwarp();
 
@@ -602,11 +659,21 @@ __global__ void estimate_ref_kernel(const float* __restrict__ qr, const float* _
   const uint8_t* r = rec + size_t(i) * (packed + 8);
   const uint32_t mask = (1u << bits) - 1u;
   float s[4] = {0.f, 0.f, 0.f, 0.f};
-  for (uint32_t j = 0; j < dim; ++j) {
-    const uint32_t bit_idx = j * bits, byte_idx = bit_idx >> 3, bit_off = bit_idx & 7;
-    uint32_t chunk = r[byte_idx];
-    if (bit_off + bits > 8 && byte_idx + 1 < packed) chunk |= uint32_t(r[byte_idx + 1]) << 8;
-    s[j & 3] = __fmaf_rn(small_u2f((chunk >> bit_off) & mask), qr[j], s[j & 3]);
+  if (bits == 8) {
+    // batch_rabitq_8bit_distance_kernel: char4 steps, chain i & 3, dims past 4*floor(dim/4) unused
+    for (uint32_t c = 0; c < dim / 4; ++c) {
+      const uint32_t word = uint32_t(r[4 * c]) | uint32_t(r[4 * c + 1]) << 8 | uint32_t(r[4 * c + 2]) << 16 |
+                            uint32_t(r[4 * c + 3]) << 24;
+      const float4 q4 = make_float4(qr[4 * c], qr[4 * c + 1], qr[4 * c + 2], qr[4 * c + 3]);
+      s[c & 3] = __fadd_rn(s[c & 3], rabitq_char4(word, q4));
+    }
+  } else {
+    for (uint32_t j = 0; j < dim; ++j) {
+      const uint32_t bit_idx = j * bits, byte_idx = bit_idx >> 3, bit_off = bit_idx & 7;
+      uint32_t chunk = r[byte_idx];
+      if (bit_off + bits > 8 && byte_idx + 1 < packed) chunk |= uint32_t(r[byte_idx + 1]) << 8;
+      s[j & 3] = __fmaf_rn(small_u2f((chunk >> bit_off) & mask), qr[j], s[j & 3]);
+    }
   }
   uint32_t a_bits = 0, r_bits = 0;
   for (int b = 0; b < 4; ++b) {
@@ -688,6 +755,7 @@ cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, uin
     case 1: return two ? occ_rch<1, 2>(rch, wpb, smem, bps) : occ_rch<1, 1>(rch, wpb, smem, bps);
     case 2: return two ? occ_rch<2, 2>(rch, wpb, smem, bps) : occ_rch<2, 1>(rch, wpb, smem, bps);
     case 4: return two ? occ_rch<4, 2>(rch, wpb, smem, bps) : occ_rch<4, 1>(rch, wpb, smem, bps);
+    case 8: return two ? occ_rch<8, 2>(rch, wpb, smem, bps) : occ_rch<8, 1>(rch, wpb, smem, bps);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -706,6 +774,9 @@ cudaError_t launch_search(const SearchArgs& a, uint32_t wpb, uint32_t blocks, cu
       break;
     case 4:
       two ? launch_rch<4, 2>(rch, a, grid, block, smem, stream) : launch_rch<4, 1>(rch, a, grid, block, smem, stream);
+      break;
+    case 8:
+      two ? launch_rch<8, 2>(rch, a, grid, block, smem, stream) : launch_rch<8, 1>(rch, a, grid, block, smem, stream);
       break;
     default:
       return cudaErrorInvalidValue;

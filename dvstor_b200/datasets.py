@@ -37,17 +37,21 @@ def gaussian_mixture(n: int, dim: int, seed, clusters: int = 1024, sigma: float 
 
 
 def low_rank_uniform(n: int, dim: int, seed, rank: int = 64, chunk: int = 1 << 16):
-    """Uniform [0,1) plus a random rank-`rank` component, scaled to unit variance."""
+    """Uniform [0,1) plus a random rank-`rank` component, standardised per dim
+    with the distribution's own mean (1/2) and variance (1/12 + the basis
+    column's squared norm), so every draw of any size shares one scaling.
+    The basis depends on the first entry of `seed` only; data and queries that
+    share it (`queries_for`) come from the same distribution."""
+    basis_seed = seed[0] if isinstance(seed, (list, tuple)) else seed
+    basis = np.random.default_rng([basis_seed, 0xBA5E]).standard_normal((rank, dim)).astype(np.float32)
+    basis /= np.float32(np.sqrt(rank))
+    sd = np.sqrt(1.0 / 12.0 + (basis.astype(np.float64) ** 2).sum(0)).astype(np.float32)
     rng = np.random.default_rng(seed)
-    basis = rng.standard_normal((rank, dim)).astype(np.float32) / np.sqrt(rank)
     out = np.empty((n, dim), np.float32)
     for s in range(0, n, chunk):
         m = min(chunk, n - s)
         x = rng.random((m, dim), dtype=np.float32) + rng.standard_normal((m, rank), dtype=np.float32) @ basis
-        out[s:s + m] = x
-    mu, sd = out.mean(0), out.std(0)
-    out -= mu
-    out /= sd
+        out[s:s + m] = (x - np.float32(0.5)) / sd
     return out
 
 

@@ -191,7 +191,10 @@ dvs_status dvs_query_prepare_tc(const float* d_query, const float* d_P, const fl
 
 /* gpu::launch_batch_rabitq_distances (src/gpu/gpu_kernel_launcher.hh:53-59):
  * n records of rabitq_size bytes each, packed back to back as the reference
- * stages them ([codes | f32 add | f32 rescale]); one query. */
+ * stages them ([codes | f32 add | f32 rescale]); one query.  bits 1, 2, 4
+ * follow batch_rabitq_distance_kernel<4,B>; bits 8 follows
+ * batch_rabitq_8bit_distance_kernel<4> (char4 steps; only the first
+ * 4*floor(dim/4) dims count, as there). */
 dvs_status dvs_rabitq_estimate(const float* d_rot_query, const float* d_factor, const uint8_t* d_records,
                                float* d_dist, uint32_t n, uint32_t dim, uint32_t bits, void* stream);
 

@@ -181,7 +181,31 @@ void query_factors(const float* qr, const float* c, uint32_t dim, uint32_t bits,
 // lane t of the tile sums dims j = t, t+4, ...; the tile is reduced with the
 // butterfly; the estimate is add_o + q.add + rescale_o * (dot + k1xSumq*(2^B-1)),
 // which nvcc contracts to fma(rescale_o, fma(k1xSumq, 2^B-1, dot), add_o + q.add).
+// batch_rabitq_8bit_distance_kernel<4> (src/gpu/kernels/distance_kernels.cuh:181-221):
+// one char4 chunk (4 dims) per step, lane t takes chunks i = t, t+4, ...; only
+// the first 4*floor(dim/4) dims take part.  Per chunk the sum
+// x0*q0 + x1*q1 + x2*q2 + x3*q3 is contracted by nvcc (left to right) to
+// fma(x3,q3, fma(x2,q2, fma(x0,q0, x1*q1))) and added to the lane's sum.
+float rabitq_estimate_8bit(const float* qr, const float* f3, const uint8_t* rec, uint32_t dim) {
+  float add_o, rescale_o;
+  std::memcpy(&add_o, rec + dim, 4);
+  std::memcpy(&rescale_o, rec + dim + 4, 4);
+  float s[4] = {0, 0, 0, 0};
+  for (uint32_t i = 0; i < dim / 4; ++i) {
+    const uint8_t* d = rec + 4 * i;
+    const float* q = qr + 4 * i;
+    float t = static_cast<float>(d[1]) * q[1];
+    t = std::fmaf(static_cast<float>(d[0]), q[0], t);
+    t = std::fmaf(static_cast<float>(d[2]), q[2], t);
+    t = std::fmaf(static_cast<float>(d[3]), q[3], t);
+    s[i & 3] = s[i & 3] + t;
+  }
+  const float dot = tile4(s);
+  return std::fmaf(rescale_o, std::fmaf(f3[1], 255.0f, dot), add_o + f3[0]);
+}
+
 float rabitq_estimate_one(const float* qr, const float* f3, const uint8_t* rec, uint32_t dim, uint32_t bits) {
+  if (bits == 8) return rabitq_estimate_8bit(qr, f3, rec, dim);
   const uint32_t packed = (bits * dim + 7) / 8;
   float add_o, rescale_o;
   std::memcpy(&add_o, rec + packed, 4);

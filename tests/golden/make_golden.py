@@ -86,6 +86,46 @@ def main(out_dir):
             outs.append(o.cpu().numpy())
         np.savez(os.path.join(out_dir, f"quantize_d{dim}_b{bits}.npz"), kind="quantize", bits=bits, x=X, P=P,
                  c_rot=c_rot, t_const=tc, out=np.stack(outs))
+    # 8-bit codes: batch_rabitq_8bit_distance_kernel reads records with char4
+    # loads, so dims are multiples of 4 (a record stride of dim + 8 bytes then
+    # keeps every load aligned).  Own seed: the fixtures above stay unchanged.
+    rng8 = np.random.default_rng(2025)
+    for dim, n in [(96, 512), (128, 256), (960, 128), (40, 256)]:
+        X = rng8.standard_normal((n, dim)).astype(np.float32)
+        X /= np.linalg.norm(X, axis=1, keepdims=True)
+        P = O.rotation_matrix(dim, 1234)
+        c_rot = O.rotate(P, O.centroid(X))
+        rec = O.quantize_batch(X, P, c_rot, O.t_const(dim, 8, 1234), 8)
+        q = rng8.standard_normal(dim).astype(np.float32)
+        q_rot, f = O.query_prepare(q, P, c_rot, 8)
+        out = torch.empty(n, dtype=torch.float32, device="cuda")
+        d_rec, d_q, d_f = dev(rec.reshape(-1)), dev(q_rot), dev(f)
+        assert lib.ref_batch_rabitq_distances(p(d_q), p(d_f), p(d_rec), p(out), n, dim, 8) == 0
+        np.savez(os.path.join(out_dir, f"rabitq_b8_d{dim}.npz"), kind="rabitq", bits=8, dim=dim, q_rot=q_rot,
+                 factor=f, records=rec, out=out.cpu().numpy())
+    for dim in (96,):
+        P = O.rotation_matrix(dim, 78)
+        c_rot = rng8.standard_normal(dim).astype(np.float32)
+        q = rng8.standard_normal(dim).astype(np.float32)
+        rq = torch.empty(dim, dtype=torch.float32, device="cuda")
+        fac = torch.empty(3, dtype=torch.float32, device="cuda")
+        assert lib.ref_query_prepare(p(dev(q)), p(dev(P)), p(dev(c_rot)), p(rq), p(fac), dim, 8) == 0
+        np.savez(os.path.join(out_dir, f"prepare_d{dim}_b8.npz"), kind="prepare", bits=8, query=q, P=P,
+                 c_rot=c_rot, q_rot=rq.cpu().numpy(), factor=fac.cpu().numpy())
+    for dim in (96,):
+        X = rng8.standard_normal((64, dim)).astype(np.float32)
+        X /= np.linalg.norm(X, axis=1, keepdims=True)
+        P = O.rotation_matrix(dim, 1234)
+        c_rot = O.rotate(P, O.centroid(X))
+        tc = O.t_const(dim, 8, 1234)
+        rs = O.rabitq_size(dim, 8)
+        outs = []
+        for x in X:
+            o = torch.zeros(rs, dtype=torch.uint8, device="cuda")
+            assert lib.ref_quantize_single(p(dev(x)), p(dev(P)), p(dev(c_rot)), p(o), dim, 8, tc) == 0
+            outs.append(o.cpu().numpy())
+        np.savez(os.path.join(out_dir, f"quantize_d{dim}_b8.npz"), kind="quantize", bits=8, x=X, P=P,
+                 c_rot=c_rot, t_const=tc, out=np.stack(outs))
     print("golden fixtures written to", out_dir)
 
 

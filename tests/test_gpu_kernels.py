@@ -41,7 +41,8 @@ def test_l2_distances_bit_exact(gpu, oracle, dim):
     np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("bits,dim", [(4, 96), (4, 128), (4, 33), (2, 96), (2, 70), (1, 128), (1, 100), (4, 960)])
+@pytest.mark.parametrize("bits,dim", [(4, 96), (4, 128), (4, 33), (2, 96), (2, 70), (1, 128), (1, 100), (4, 960),
+                                      (8, 96), (8, 960), (8, 30), (8, 130)])
 def test_rabitq_estimate_bit_exact(gpu, oracle, bits, dim):
     import torch
 

@@ -29,6 +29,11 @@ def cases(oracle, tmp_path_factory):
         "r48": Case(oracle, tmp, "r48", normalized_gaussian(3000, 64, 4), 48, 64),
         "bits2": Case(oracle, tmp, "bits2", normalized_gaussian(2000, 40, 5), 16, 32, bits=2),
         "bits1": Case(oracle, tmp, "bits1", normalized_gaussian(2000, 64, 6), 16, 32, bits=1),
+        "bits8": Case(oracle, tmp, "bits8", normalized_gaussian(2000, 64, 13), 16, 32, bits=8),
+        "bits8d30": Case(oracle, tmp, "bits8d30", normalized_gaussian(1500, 30, 14), 16, 32, bits=8),
+        "bits8d160": Case(oracle, tmp, "bits8d160", normalized_gaussian(1200, 160, 15), 24, 32, bits=8),
+        "bits2d520": Case(oracle, tmp, "bits2d520", normalized_gaussian(800, 520, 16), 16, 32, bits=2),
+        "bits1d1040": Case(oracle, tmp, "bits1d1040", normalized_gaussian(600, 1040, 17), 16, 32, bits=1),
         "ragged": Case(oracle, tmp, "ragged", normalized_gaussian(1500, 30, 7), 16, 32),
         "ip": Case(oracle, tmp, "ip", normalized_gaussian(2000, 48, 8), 16, 32, metric="ip"),
         "shards": Case(oracle, tmp, "shards", uniform_int_data(3000, 32, 9), 24, 48, M=3),
@@ -50,8 +55,9 @@ def run_both(gpu, oracle, case, Q, k, L, mode="rabitq_gpu"):
 
 
 @pytest.mark.parametrize("name,L", [("int128", 64), ("gauss96", 64), ("gauss96", 128), ("r48", 100), ("bits2", 32),
-                                    ("bits1", 48), ("ragged", 40), ("ip", 32), ("shards", 64), ("d160", 40),
-                                    ("d256r48", 48), ("d960r48", 200)])
+                                    ("bits1", 48), ("bits8", 48), ("bits8d30", 32), ("ragged", 40), ("ip", 32),
+                                    ("shards", 64), ("d160", 40), ("d256r48", 48), ("d960r48", 200),
+                                    ("bits8d160", 40), ("bits2d520", 32), ("bits1d1040", 32)])
 @pytest.mark.parametrize("mode", ["rabitq_gpu", "exact_gpu"])
 def test_search_matches_oracle(gpu, oracle, cases, name, L, mode):
     case = cases[name]
@@ -59,7 +65,7 @@ def test_search_matches_oracle(gpu, oracle, cases, name, L, mode):
     if name in ("int128", "shards"):
         Q = uniform_int_data(300, d, 99)
     elif name == "d960r48":
-        Q = low_rank_uniform(300, d, 99)
+        Q = low_rank_uniform(300, d, [4, 99])
     else:
         Q = normalized_gaussian(300, d, 99)
     k = 10
@@ -74,7 +80,7 @@ def test_search_matches_oracle(gpu, oracle, cases, name, L, mode):
 def test_k100_wide_records(gpu, oracle, cases, mode):
     """k = 100 at beam width 200 on D = 960, R = 48 (488-byte codes)."""
     case = cases["d960r48"]
-    Q = low_rank_uniform(120, 960, 98)
+    Q = low_rank_uniform(120, 960, [4, 98])
     ids, d, st, o_ids, o_d, o_cnt, b_ids, b_d = run_both(gpu, oracle, case, Q, 100, 200, mode)
     assert_results_match(ids, d, o_ids, o_d, b_ids, b_d)
     assert st["estimates"] == int(o_cnt[:, 1].sum())
