@@ -40,10 +40,6 @@ __device__ __forceinline__ float l2_quad_partial(const float* __restrict__ q, co
   const float4* x4 = reinterpret_cast<const float4*>(x);
   float acc = 0.f;
   uint32_t i = t;
-  // four chunks per trip keep four independent loads in flight
-  for (; i + 12 < n4; i += 16) {
-    const float4 a0 = __ldg(x4 + i), a1 = __ldg(x4 + i + 4), a2 = __ldg(x4 + i + 8), a3 = __ldg(x4 + i + 12);
-    const float4 b0 = q4[i], b1 = q4[i + 4], b2 = q4[i + 8], b3 = q4[i + 12];
 #define DVS_ACC4(B, A)                                   \
   {                                                      \
     float d;                                             \
@@ -52,6 +48,21 @@ __device__ __forceinline__ float l2_quad_partial(const float* __restrict__ q, co
     d = __fsub_rn(B.z, A.z); acc = __fmaf_rn(d, d, acc); \
     d = __fsub_rn(B.w, A.w); acc = __fmaf_rn(d, d, acc); \
   }
+  // long rows: eight chunks per trip in flight
+  for (; i + 28 < n4; i += 32) {
+    float4 a[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = __ldg(x4 + i + 4 * k);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 b = q4[i + 4 * k];
+      DVS_ACC4(b, a[k])
+    }
+  }
+  // four chunks per trip keep four independent loads in flight
+  for (; i + 12 < n4; i += 16) {
+    const float4 a0 = __ldg(x4 + i), a1 = __ldg(x4 + i + 4), a2 = __ldg(x4 + i + 8), a3 = __ldg(x4 + i + 12);
+    const float4 b0 = q4[i], b1 = q4[i + 4], b2 = q4[i + 8], b3 = q4[i + 12];
     DVS_ACC4(b0, a0) DVS_ACC4(b1, a1) DVS_ACC4(b2, a2) DVS_ACC4(b3, a3)
   }
   for (; i < n4; i += 4) {

@@ -219,28 +219,31 @@ __device__ __forceinline__ float estimate_quad_chain(const DevLayout& ix, uint32
   }
   float s = 0.f;
   if constexpr (BITS == 8) {
+    // lane t takes words t, t+4, ...: 16 of them in flight per batch
     const uint32_t nw = ix.dim >> 2;
-    uint32_t w = t;
-    for (; w + 12 < nw; w += 16) {
-      const uint32_t a0 = __ldg(r + w), a1 = __ldg(r + w + 4), a2 = __ldg(r + w + 8), a3 = __ldg(r + w + 12);
-      s = __fadd_rn(s, rabitq_char4(a0, *reinterpret_cast<const float4*>(qr + 4 * w)));
-      s = __fadd_rn(s, rabitq_char4(a1, *reinterpret_cast<const float4*>(qr + 4 * (w + 4))));
-      s = __fadd_rn(s, rabitq_char4(a2, *reinterpret_cast<const float4*>(qr + 4 * (w + 8))));
-      s = __fadd_rn(s, rabitq_char4(a3, *reinterpret_cast<const float4*>(qr + 4 * (w + 12))));
+    for (uint32_t w0 = t; w0 < nw; w0 += 64) {
+      uint32_t a[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (w0 + 4 * k < nw) a[k] = __ldg(r + w0 + 4 * k);
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (w0 + 4 * k < nw)
+          s = __fadd_rn(s, rabitq_char4(a[k], *reinterpret_cast<const float4*>(qr + 4 * (w0 + 4 * k))));
     }
-    for (; w < nw; w += 4) s = __fadd_rn(s, rabitq_char4(__ldg(r + w), *reinterpret_cast<const float4*>(qr + 4 * w)));
   } else {
     constexpr uint32_t kPer = 32 / BITS, kMask = (1u << BITS) - 1u;
     const uint4* r4 = reinterpret_cast<const uint4*>(r);
     const uint32_t nch = (ix.dim / kPer) >> 2;  // 16-byte chunks whose every dim is < dim
     const uint32_t sh0 = BITS * t;
-    for (uint32_t ch = 0; ch < nch; ch += 4) {
-      uint4 v[4];
+    // 16 chunks (256 bytes of codes) in flight per batch
+    for (uint32_t ch = 0; ch < nch; ch += 16) {
+      uint4 v[16];
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
+      for (int k = 0; k < 16; ++k)
         if (ch + k < nch) v[k] = __ldg(r4 + ch + k);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 16; ++k) {
         if (ch + k < nch) {
           const uint32_t wv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
