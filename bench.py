@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--cache", default=os.environ.get("DVS_BENCH_CACHE", "/tmp/dvs_b200_bench"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--placement", choices=["replicate", "shard"], default="replicate",
+                    help="shard: one process over --gpus devices, the index split by slot (run without torchrun)")
     return ap.parse_args()
 
 
@@ -431,10 +433,119 @@ def run_ours(args):
     dist.close()
 
 
+def run_sharded(args):
+    """One process over --gpus devices with the index split by slot (placement
+    "shard": node g on device g mod N, remote rows read from peer HBM).  Every
+    device searches its own batch per step on its own stream; time = max over
+    devices of the CUDA-event time."""
+    import torch
+
+    import dvstor_b200 as D
+    from dvstor_b200 import datasets
+
+    ngpu = args.gpus
+    dist = Dist("gloo")
+    wp = workload_params(args.workload, args.n)
+    L = args.beam_width or wp["search_L"]
+    k, B = args.k, args.batch
+    prefix = ensure_index(args, wp, 0, dist)
+    ix = D.Index(prefix, devices=tuple(range(ngpu)), placement="shard")
+    info = ix.info
+    nsteps = args.warmup + args.steps
+    Qpool = datasets.queries_for(args.workload, B * ngpu * nsteps)
+    per = Qpool.reshape(nsteps, ngpu, B, wp["dim"])
+    dq = [torch.from_numpy(np.ascontiguousarray(per[:, d])).to(f"cuda:{d}") for d in range(ngpu)]
+    outs = [(torch.empty((B, k), dtype=torch.int32, device=f"cuda:{d}"),
+             torch.empty((B, k), dtype=torch.float32, device=f"cuda:{d}"),
+             torch.zeros((B, 4), dtype=torch.int32, device=f"cuda:{d}")) for d in range(ngpu)]
+    streams = [torch.cuda.Stream(device=d) for d in range(ngpu)]
+
+    def step(s):
+        for d in range(ngpu):
+            with torch.cuda.device(d):
+                ix.search_device(dq[d][s], k, L, d_out_ids=outs[d][0], d_out_dist=outs[d][1], d_counters=outs[d][2],
+                                 stream=streams[d], device_slot=d)
+
+    for s in range(args.warmup):
+        step(s)
+    for d in range(ngpu):
+        torch.cuda.synchronize(d)
+    ix.set_kernel_timing(True)
+    for d in range(ngpu):
+        ix.kernel_times(d)
+    sampler = clocks_sampler(0)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(ngpu)]
+    t_wall0 = time.time()
+    for d in range(ngpu):
+        ev[d][0].record(streams[d])
+    for s in range(args.steps):
+        step(args.warmup + s)
+    for d in range(ngpu):
+        ev[d][1].record(streams[d])
+    for d in range(ngpu):
+        torch.cuda.synchronize(d)
+    t_wall1 = time.time()
+    clocks = clocks_summary(sampler, t_wall0, t_wall1)
+    ms = max(ev[d][0].elapsed_time(ev[d][1]) for d in range(ngpu))
+    ktimes = [ix.kernel_times(d) for d in range(ngpu)]
+    ix.set_kernel_timing(False)
+    value = ngpu * B * args.steps / (ms / 1e3)
+    c = np.concatenate([outs[d][2].cpu().numpy() for d in range(ngpu)]).astype(np.int64)
+    H, E, Cr = c[:, 0].mean(), c[:, 1].mean(), c[:, 2].mean()
+    bq = bytes_per_query(info.dim, info.R, info.rabitq_bits, k, H, E, Cr, B)
+    search_avg_ms = max(st / max(n, 1) for n, _, st in ktimes)
+    achieved = bq * B * ngpu / (search_avg_ms / 1e3) / 1e9
+    peak, peak_kind = hbm_peak()
+
+    # end to end: dvs_search splits a host batch over the devices
+    hq = torch.empty((B * ngpu, wp["dim"]), dtype=torch.float32, pin_memory=True)
+    h_ids = torch.empty((B * ngpu, k), dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
+    h_d = torch.empty((B * ngpu, k), dtype=torch.float32, pin_memory=True).numpy()
+    from dvstor_b200._lib import check, lib, ptr
+
+    def host_search(q):
+        hq.numpy()[:] = q
+        check(lib().dvs_search(ix._h, ptr(hq.numpy()), B * ngpu, wp["dim"], k, L, 0, ptr(h_ids), ptr(h_d), None))
+
+    host_search(per[0].reshape(-1, wp["dim"]))
+    t = time.perf_counter()
+    for s in range(args.steps):
+        host_search(per[(args.warmup + s) % nsteps].reshape(-1, wp["dim"]))
+    e2e = ngpu * B * args.steps / (time.perf_counter() - t)
+
+    gtq = Qpool[:1000]
+    g_ids, _ = ix.search(gtq, k, L)
+    Xv = ix.download()[2]
+    rec = recall(g_ids, ground_truth(Xv, gtq, k, 0))
+    ix.close()
+    line = {
+        "metric": f"queries/sec at recall@10 parity (k={k}, L={L})", "value": value, "unit": "queries/s",
+        "n_gpus": ngpu, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"], "build_L": wp["build_L"],
+                   "rabitq_bits": 4, "k": k, "beam_width": L, "queries_per_step_per_gpu": B,
+                   "parallelism": f"shard x{ngpu} (one process, peer HBM reads)",
+                   "l2": f"index {index_device_bytes(info) / 1e9:.2f} GB split over {ngpu} GPUs, not flushed"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * ngpu, "unit": "GB/s",
+                     "frac": achieved / (peak * ngpu), "traffic": None,
+                     "peak_source": f"{peak_kind} hbm_gbs x {ngpu} GPUs", "kernel": "search_kernel",
+                     "kernel_ms": search_avg_ms, "bytes_per_query": bq, "per_query": {"H": H, "E": E, "C_r": Cr}},
+        "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": B * ngpu * wp["dim"] * 4,
+                "d2h_bytes_per_step": B * ngpu * k * 8},
+        "gpu_launches": 2 * args.steps * ngpu,
+        "clocks": clocks,
+        "recall_at_10": rec,
+        "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.placement == "shard":
+        run_sharded(args)
     else:
         run_ours(args)
 

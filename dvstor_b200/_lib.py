@@ -29,7 +29,8 @@ EXPORTED = (
     "dvs_set_hop_limit", "dvs_set_visited_slots", "dvs_query_prepare", "dvs_rabitq_estimate", "dvs_l2_distances", "dvs_host_index_load",
     "dvs_host_index_info", "dvs_host_index_arrays", "dvs_host_index_free", "dvs_write_index", "dvs_last_error",
     "dvs_status_string", "dvs_device_count", "dvs_build_index", "dvs_set_kernel_timing", "dvs_kernel_times",
-    "dvs_search_device_noalloc", "dvs_set_rotation", "dvs_query_prepare_tc",
+    "dvs_search_device_noalloc", "dvs_set_rotation", "dvs_query_prepare_tc", "dvs_create", "dvs_reserve",
+    "dvs_insert",
 )
 
 
@@ -65,6 +66,21 @@ class WriteParams(C.Structure):
                 ("beam_width", C.c_uint32), ("alpha", C.c_double), ("metric", C.c_int), ("t_const", C.c_double)]
 
 
+class CreateParams(C.Structure):
+    _fields_ = [("dim", C.c_uint32), ("R", C.c_uint32), ("rabitq_bits", C.c_uint32), ("metric", C.c_int),
+                ("rotation", C.c_void_p), ("rotated_centroid", C.c_void_p), ("t_const", C.c_double),
+                ("devices", C.POINTER(C.c_int)), ("num_devices", C.c_uint32), ("capacity", C.c_uint64)]
+
+
+class InsertParams(C.Structure):
+    _fields_ = [("beam_width_construction", C.c_uint32), ("alpha", C.c_float), ("max_batch", C.c_uint32)]
+
+
+class InsertStats(C.Structure):
+    _fields_ = [("inserted", C.c_uint64), ("steps", C.c_uint64), ("expansions", C.c_uint64),
+                ("distances", C.c_uint64), ("full_prunes", C.c_uint64), ("device_ms", C.c_float)]
+
+
 _lib = None
 
 
@@ -98,6 +114,9 @@ def lib():
             "dvs_host_index_arrays": [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
                                       C.POINTER(vp)],
             "dvs_write_index": [C.POINTER(WriteParams), vp, vp, vp, vp, vp],
+            "dvs_create": [C.POINTER(CreateParams), C.POINTER(vp)],
+            "dvs_reserve": [vp, u64],
+            "dvs_insert": [vp, vp, vp, u32, u32, C.POINTER(InsertParams), C.POINTER(InsertStats)],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)

@@ -14,98 +14,12 @@
 #include <thread>
 #include <vector>
 
-#include "internal.h"
-#include "search.cuh"
+#include "index_state.h"
 
 using dvs::fail;
 
 namespace dvs {
 namespace {
-
-#define DVS_CUDA(call)                                                                             \
-  do {                                                                                             \
-    const cudaError_t e_ = (call);                                                                 \
-    if (e_ != cudaSuccess) {                                                                       \
-      return fail(e_ == cudaErrorMemoryAllocation ? DVS_ERR_OOM : DVS_ERR_CUDA,                    \
-                  std::string(#call) + ": " + cudaGetErrorString(e_));                             \
-    }                                                                                              \
-  } while (0)
-
-template <class T>
-void dev_free(T*& p) {
-  if (p) cudaFree(p);
-  p = nullptr;
-}
-
-// Visited-set sizing: default shared-memory slots per beam entry (32-bit table
-// for indexes of 2^24 nodes or more, compact 16-bit table below) and the spill table.
-constexpr uint32_t kDefaultSlots32 = 48;
-constexpr uint32_t kDefaultSlots16 = 48;
-constexpr uint32_t kOverflowSlots = 1u << 14;
-
-struct Device {
-  int ordinal = 0;
-  cudaStream_t stream = nullptr;
-  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-  uint32_t sm_count = 0;
-  uint32_t shard = 0;     // shard held (sharded placement), rows = its row count
-  uint64_t rows = 0;
-  // index
-  uint32_t* adj = nullptr;
-  uint32_t* rec = nullptr;
-  float* vecs = nullptr;
-  uint32_t* ids = nullptr;
-  float* P = nullptr;
-  float* c_rot = nullptr;
-  DevLayout lay;
-  // scratch
-  size_t q_cap = 0;        // queries the scratch holds
-  size_t out_cap = 0;      // result slots the host-path buffers hold
-  float* queries = nullptr;
-  float* qrot = nullptr;
-  float* qfac = nullptr;
-  uint32_t* out_ids = nullptr;
-  float* out_dist = nullptr;
-  uint32_t* counters = nullptr;
-  uint32_t* work = nullptr;
-  uint32_t* ovf = nullptr;
-  size_t ovf_slots = 0;
-  // kernel timing ring: (before prepare, after prepare, after search)
-  static constexpr size_t kRing = 4096;
-  std::vector<cudaEvent_t> tev;
-  size_t tcount = 0;
-
-  void release() {
-    if (ordinal < 0) return;
-    cudaSetDevice(ordinal);
-    dev_free(adj);
-    dev_free(rec);
-    dev_free(vecs);
-    dev_free(ids);
-    dev_free(P);
-    dev_free(c_rot);
-    dev_free(queries);
-    dev_free(qrot);
-    dev_free(qfac);
-    dev_free(out_ids);
-    dev_free(out_dist);
-    dev_free(counters);
-    dev_free(work);
-    dev_free(ovf);
-    if (ev0) cudaEventDestroy(ev0);
-    if (ev1) cudaEventDestroy(ev1);
-    for (cudaEvent_t e : tev) cudaEventDestroy(e);
-    tev.clear();
-    if (stream) cudaStreamDestroy(stream);
-    ev0 = ev1 = nullptr;
-    stream = nullptr;
-  }
-};
-
-struct LaunchShape {
-  uint32_t cap = 0, cap_pad = 0, hcap = 0, wpb = 0, blocks_per_sm = 0;
-  uint32_t vt16 = 0, hbuckets = 0, hlimit = 0;
-};
 
 // Uploads the rows of shard `shard` of `nshard` (slot g with g mod nshard ==
 // shard, local row g / nshard; nshard == 1 uploads everything).
@@ -153,6 +67,7 @@ dvs_status upload(Device& d, const HostIndex& h, uint32_t shard, uint32_t nshard
   DVS_CUDA(cudaMalloc(&d.work, 16));
   d.shard = shard;
   d.rows = nl;
+  d.cap_rows = nl;
   DevLayout& L = d.lay;
   L.adj = d.adj;
   L.rec = d.rec;
@@ -207,6 +122,8 @@ dvs_status link_shards(std::vector<Device>& devs) {
   }
   return DVS_OK;
 }
+
+}  // namespace
 
 dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path) {
   const size_t vs = d.lay.vec_stride;
@@ -272,28 +189,28 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, Launc
   return DVS_OK;
 }
 
-}  // namespace
 }  // namespace dvs
 
-struct dvs_index {
-  dvs::HostIndex host;              // kept for downloads and metadata
-  std::vector<dvs::Device> devs;
-  uint32_t hop_limit = 0;
-  uint32_t slots_per_entry = 0;  // 0 = the default of the table kind in use
-  bool kernel_timing = false;
-  dvs_rotation rotation = DVS_ROTATION_EXACT;
-  std::mutex mu;
-};
 
 namespace dvs {
-namespace {
 
 // Prepare + search for nq device-resident queries on one device.
 dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L, dvs_mode mode,
-                     uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st, bool timed) {
+                     uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st, bool timed,
+                     bool out_slots) {
   const DevLayout& lay = d.lay;
   const bool rabitq = mode == DVS_MODE_RABITQ_GPU;
   if (lay.R > 64) return fail(DVS_ERR_UNSUPPORTED, "max out-degree above 64 is not supported by the search kernel");
+  if (lay.n == 0) {
+    // an index created empty and not yet inserted into: every result slot is empty
+    if (timed) DVS_CUDA(cudaEventRecord(d.ev0, st));
+    DVS_CUDA(cudaMemsetAsync(d_ids, 0xFF, size_t(nq) * k * 4, st));
+    DVS_CUDA(launch_fill_f32(d_dist, size_t(nq) * k, __builtin_huge_valf(), st));
+    if (d_counters) DVS_CUDA(cudaMemsetAsync(d_counters, 0, size_t(nq) * 16, st));
+    DVS_CUDA(cudaMemsetAsync(d.work, 0, 16, st));
+    if (timed) DVS_CUDA(cudaEventRecord(d.ev1, st));
+    return DVS_OK;
+  }
   const uint32_t cap = rabitq ? L + kBeamSlack : L;
   LaunchShape s;
   dvs_status rc = launch_shape(d, cap, ix->slots_per_entry, s);
@@ -354,11 +271,14 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
   a.inv_hbuckets = s.hbuckets ? 1.0f / float(s.hbuckets) : 0.f;
   a.cap_pad = s.cap_pad;
   a.dim_pad = lay.vec_stride;
+  a.out_slots = out_slots ? 1u : 0u;
   DVS_CUDA(launch_search(a, s.wpb, blocks, st));
   if (tr) DVS_CUDA(cudaEventRecord(tr[2], st));
   if (timed) DVS_CUDA(cudaEventRecord(d.ev1, st));
   return DVS_OK;
 }
+
+namespace {
 
 dvs_status check_query_args(const dvs_index* ix, uint32_t nq, uint32_t dim, uint32_t k, uint32_t L, dvs_mode mode) {
   if (!ix) return fail(DVS_ERR_ARG, "null index");
@@ -432,6 +352,53 @@ dvs_status dvs_open(const dvs_open_params* p, dvs_index** out) {
                   : dvs::upload(ix->devs[i], ix->host, 0, 1);
     }
     if (s == DVS_OK && sharded) s = dvs::link_shards(ix->devs);
+  }
+  if (s != DVS_OK) {
+    for (auto& d : ix->devs) d.release();
+    delete ix;
+    return s;
+  }
+  *out = ix;
+  return DVS_OK;
+}
+
+dvs_status dvs_create(const dvs_create_params* p, dvs_index** out) {
+  if (!p || !out || !p->rotation || !p->rotated_centroid) return fail(DVS_ERR_ARG, "null argument");
+  *out = nullptr;
+  if (p->dim == 0) return fail(DVS_ERR_DIM, "dim must be > 0");
+  if (p->R == 0 || p->R > 64) return fail(DVS_ERR_ARG, "R must be in 1..64");
+  if (p->rabitq_bits != 1 && p->rabitq_bits != 2 && p->rabitq_bits != 4 && p->rabitq_bits != 8)
+    return fail(DVS_ERR_BITS, "rabitq_bits must be 1, 2, 4, or 8");
+  if (p->metric != DVS_METRIC_L2 && p->metric != DVS_METRIC_IP) return fail(DVS_ERR_ARG, "metric must be l2 or ip");
+  const int ndev_vis = dvs_device_count();
+  if (ndev_vis == 0) return fail(DVS_ERR_NO_DEVICE, "no CUDA device is visible");
+  const uint32_t nd = p->num_devices ? p->num_devices : 1;
+  std::vector<int> devs;
+  for (uint32_t i = 0; i < nd; ++i) {
+    const int o = p->devices ? p->devices[i] : int(i);
+    if (o < 0 || o >= ndev_vis) return fail(DVS_ERR_ARG, "device ordinal " + std::to_string(o) + " is not visible");
+    devs.push_back(o);
+  }
+  auto* ix = new (std::nothrow) dvs_index;
+  if (!ix) return fail(DVS_ERR_OOM, "host allocation failed");
+  dvs_index_info& in = ix->host.info;
+  in.num_vectors = 0;
+  in.dim = p->dim;
+  in.R = p->R;
+  in.rabitq_bits = p->rabitq_bits;
+  in.rabitq_size = (p->rabitq_bits * p->dim + 7) / 8 + 8;
+  in.num_memory_nodes = 1;
+  in.medoid = 0;
+  in.metric = p->metric;
+  in.t_const = p->t_const;
+  ix->host.rotation.assign(p->rotation, p->rotation + size_t(p->dim) * p->dim);
+  ix->host.rotated_centroid.assign(p->rotated_centroid, p->rotated_centroid + p->dim);
+  dvs_status s = DVS_OK;
+  ix->devs.resize(devs.size());
+  for (size_t i = 0; i < devs.size() && s == DVS_OK; ++i) {
+    ix->devs[i].ordinal = devs[i];
+    s = dvs::upload(ix->devs[i], ix->host, 0, 1);
+    if (s == DVS_OK) s = dvs::grow_rows(ix->devs[i], p->capacity ? p->capacity : 1024);
   }
   if (s != DVS_OK) {
     for (auto& d : ix->devs) d.release();

@@ -1,0 +1,128 @@
+// Host-side state of an open index, shared by the translation units that
+// implement the C ABI (api.cu: open, search, kernel entry points; insert.cu:
+// create and online insert).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+#include "search.cuh"
+
+struct dvs_index;
+
+namespace dvs {
+
+#define DVS_CUDA(call)                                                                             \
+  do {                                                                                             \
+    const cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess) {                                                                       \
+      return fail(e_ == cudaErrorMemoryAllocation ? DVS_ERR_OOM : DVS_ERR_CUDA,                    \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                             \
+    }                                                                                              \
+  } while (0)
+
+template <class T>
+void dev_free(T*& p) {
+  if (p) cudaFree(p);
+  p = nullptr;
+}
+
+// Visited-set sizing: default shared-memory slots per beam entry (32-bit table
+// for indexes of 2^24 nodes or more, compact 16-bit table below) and the spill table.
+constexpr uint32_t kDefaultSlots32 = 48;
+constexpr uint32_t kDefaultSlots16 = 48;
+constexpr uint32_t kOverflowSlots = 1u << 14;
+
+struct Device {
+  int ordinal = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  uint32_t sm_count = 0;
+  uint32_t shard = 0;     // shard held (sharded placement), rows = its row count
+  uint64_t rows = 0;
+  uint64_t cap_rows = 0;  // rows the index arrays have room for (online insert grows them)
+  // index
+  uint32_t* adj = nullptr;
+  uint32_t* rec = nullptr;
+  float* vecs = nullptr;
+  uint32_t* ids = nullptr;
+  float* P = nullptr;
+  float* c_rot = nullptr;
+  DevLayout lay;
+  // scratch
+  size_t q_cap = 0;        // queries the scratch holds
+  size_t out_cap = 0;      // result slots the host-path buffers hold
+  float* queries = nullptr;
+  float* qrot = nullptr;
+  float* qfac = nullptr;
+  uint32_t* out_ids = nullptr;
+  float* out_dist = nullptr;
+  uint32_t* counters = nullptr;
+  uint32_t* work = nullptr;
+  uint32_t* ovf = nullptr;
+  size_t ovf_slots = 0;
+  // kernel timing ring: (before prepare, after prepare, after search)
+  static constexpr size_t kRing = 4096;
+  std::vector<cudaEvent_t> tev;
+  size_t tcount = 0;
+
+  void release() {
+    if (ordinal < 0) return;
+    cudaSetDevice(ordinal);
+    dev_free(adj);
+    dev_free(rec);
+    dev_free(vecs);
+    dev_free(ids);
+    dev_free(P);
+    dev_free(c_rot);
+    dev_free(queries);
+    dev_free(qrot);
+    dev_free(qfac);
+    dev_free(out_ids);
+    dev_free(out_dist);
+    dev_free(counters);
+    dev_free(work);
+    dev_free(ovf);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    for (cudaEvent_t e : tev) cudaEventDestroy(e);
+    tev.clear();
+    if (stream) cudaStreamDestroy(stream);
+    ev0 = ev1 = nullptr;
+    stream = nullptr;
+  }
+};
+
+struct LaunchShape {
+  uint32_t cap = 0, cap_pad = 0, hcap = 0, wpb = 0, blocks_per_sm = 0;
+  uint32_t vt16 = 0, hbuckets = 0, hlimit = 0;
+};
+
+// Search-kernel launch shape for beam capacity `cap` on device `d`.
+dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, LaunchShape& s);
+// Grows the device's query scratch to nq queries (and nq*k results for host calls).
+dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path);
+// Prepare + search for nq device-resident queries on one device (asynchronous on st).
+dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L, dvs_mode mode,
+                     uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st, bool timed,
+                     bool out_slots = false);
+
+// Grows the device arrays of a replicated index to hold `rows` nodes (online insert).
+dvs_status grow_rows(Device& d, uint64_t rows);
+
+}  // namespace dvs
+
+struct dvs_index {
+  dvs::HostIndex host;              // kept for downloads and metadata
+  std::vector<dvs::Device> devs;
+  uint32_t hop_limit = 0;
+  uint32_t slots_per_entry = 0;  // 0 = the default of the table kind in use
+  bool kernel_timing = false;
+  dvs_rotation rotation = DVS_ROTATION_EXACT;
+  std::mutex mu;
+};

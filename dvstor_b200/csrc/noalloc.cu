@@ -90,6 +90,15 @@ extern "C" dvs_status dvs_search_device_noalloc(dvs_index* index, uint32_t devic
 
   cudaError_t e = cudaSetDevice(v.ordinal);
   if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+  if (lay.n == 0) {
+    // an index created empty and not yet inserted into: every result slot is empty
+    cudaStream_t st0 = static_cast<cudaStream_t>(stream);
+    e = cudaMemsetAsync(d_out_ids, 0xFF, size_t(nq) * k * 4, st0);
+    if (e == cudaSuccess) e = launch_fill_f32(d_out_dist, size_t(nq) * k, __builtin_huge_valf(), st0);
+    if (e == cudaSuccess && d_counters) e = cudaMemsetAsync(d_counters, 0, size_t(nq) * 16, st0);
+    if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("empty-index result fill: ") + cudaGetErrorString(e));
+    return DVS_OK;
+  }
   unsigned char* base = nullptr;
   s = scratch_address(v.ordinal, &base);
   if (s != DVS_OK) return s;

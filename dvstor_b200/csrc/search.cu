@@ -628,7 +628,8 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
       }
     } else {
       for (uint32_t p = lane; p < nb && p < a.k; p += 32) {
-        a.out_ids[size_t(qi) * a.k + p] = ix.ids[bi[p] & ~kExpandedBit];
+        const uint32_t slot = bi[p] & ~kExpandedBit;
+        a.out_ids[size_t(qi) * a.k + p] = a.out_slots ? slot : ix.ids[slot];
         a.out_dist[size_t(qi) * a.k + p] = bd[p];
       }
     }
@@ -791,6 +792,17 @@ cudaError_t launch_estimate_ref_layout(const float* qrot, const float* f3, const
                                        uint32_t n, uint32_t dim, uint32_t bits, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   estimate_ref_kernel<<<(n + 127) / 128, 128, 0, stream>>>(qrot, f3, records, out, n, dim, bits);
+  return cudaGetLastError();
+}
+
+__global__ void fill_f32_kernel(float* p, size_t n, float v) {
+  const size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = v;
+}
+
+cudaError_t launch_fill_f32(float* p, size_t n, float v, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  fill_f32_kernel<<<uint32_t((n + 255) / 256), 256, 0, stream>>>(p, n, v);
   return cudaGetLastError();
 }
 

@@ -66,6 +66,7 @@ struct SearchArgs {
   uint32_t hbuckets = 0;            // its bucket count (8 entries each)
   float inv_hbuckets = 0.f;
   uint32_t cap_pad = 0, dim_pad = 0;
+  uint32_t out_slots = 0;           // 1: results are dense slots (online insert), else stored node ids
 };
 
 // What another translation unit may read of an open index's device copy.
@@ -128,5 +129,6 @@ cudaError_t launch_estimate_ref_layout(const float* qrot, const float* f3, const
                                        uint32_t n, uint32_t dim, uint32_t bits, cudaStream_t stream);
 cudaError_t launch_l2_rows(const float* q, const float* cand, float* out, uint32_t n, uint32_t dim,
                            cudaStream_t stream);
+cudaError_t launch_fill_f32(float* p, size_t n, float v, cudaStream_t stream);
 
 }  // namespace dvs

@@ -24,9 +24,12 @@ def normalized_gaussian(n: int, dim: int, seed, chunk: int = 1 << 18) -> np.ndar
 
 def gaussian_mixture(n: int, dim: int, seed, clusters: int = 1024, sigma: float = 20.0, chunk: int = 1 << 18):
     """Mixture of `clusters` Gaussians: centres uniform in [0,255]^dim, per-cluster
-    sigma, clipped to [0,255] and rounded to integers."""
+    sigma, clipped to [0,255] and rounded to integers.  The centres depend on
+    the first entry of `seed` only, so queries drawn with a longer seed
+    (`queries_for`) come from the same mixture as the data."""
+    centre_seed = seed[0] if isinstance(seed, (list, tuple)) else seed
+    centres = np.random.default_rng([centre_seed, 0xCE]).uniform(0, 255, size=(clusters, dim)).astype(np.float32)
     rng = np.random.default_rng(seed)
-    centres = rng.uniform(0, 255, size=(clusters, dim)).astype(np.float32)
     out = np.empty((n, dim), np.float32)
     for s in range(0, n, chunk):
         m = min(chunk, n - s)

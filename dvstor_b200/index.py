@@ -40,6 +40,56 @@ class Index:
         self.info = info
         self.dim = info.dim
 
+    @classmethod
+    def create(cls, dim: int, R: int, rotation, rotated_centroid, t_const: float, rabitq_bits: int = 4,
+               metric: str = "l2", devices=(0,), capacity: int = 0) -> "Index":
+        """An empty index on `devices` (``dvs_create``) that inserts grow; the
+        first insert becomes the medoid (src/vamana/vamana.hh:479-546)."""
+        P = np.ascontiguousarray(rotation, np.float32).reshape(-1)
+        c = np.ascontiguousarray(rotated_centroid, np.float32).reshape(-1)
+        if P.size != dim * dim or c.size != dim:
+            raise ValueError("rotation must be dim*dim and the rotated centroid dim floats")
+        devs = (C.c_int * len(devices))(*devices)
+        p = _lib.CreateParams(dim, R, rabitq_bits, _lib.METRIC[metric], ptr(P), ptr(c), float(t_const), devs,
+                              len(devices), capacity)
+        h = C.c_void_p()
+        check(lib().dvs_create(C.byref(p), C.byref(h)))
+        self = cls.__new__(cls)
+        self._h = h
+        self.devices = tuple(devices)
+        self.refresh_info()
+        return self
+
+    def refresh_info(self) -> None:
+        info = _lib.IndexInfo()
+        check(lib().dvs_index_get_info(self._h, C.byref(info)))
+        self.info = info
+        self.dim = info.dim
+
+    def reserve(self, capacity: int) -> None:
+        check(lib().dvs_reserve(self._h, capacity))
+
+    def insert(self, vectors, ids=None, beam_width_construction: int = 200, alpha: float = 1.2,
+               max_batch: int = 1024) -> dict:
+        """dvs_insert: Vamana::insert (src/vamana/vamana.hh:458-999) for a batch,
+        in steps of min(max_batch, node count) vectors that each search the graph
+        of the step's start.  Returns the insert statistics."""
+        X = np.ascontiguousarray(vectors, dtype=np.float32)
+        if X.ndim == 1:
+            X = X[None]
+        n = X.shape[0]
+        idp = None
+        if ids is not None:
+            idp = np.ascontiguousarray(ids, dtype=np.uint32)
+            if idp.shape != (n,):
+                raise ValueError("ids must have one entry per vector")
+        prm = _lib.InsertParams(beam_width_construction, alpha, max_batch)
+        st = _lib.InsertStats()
+        check(lib().dvs_insert(self._h, ptr(X), ptr(idp) if idp is not None else None, n, X.shape[1], C.byref(prm),
+                               C.byref(st)))
+        self.refresh_info()
+        return {f: getattr(st, f) for f, _ in _lib.InsertStats._fields_}
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib().dvs_close(self._h)
@@ -157,6 +207,21 @@ class ComputeService:
         ids, _ = self.search_batch(np.asarray(query, np.float32)[None], k)
         row = ids[0]
         return [int(x) for x in row if x != _lib.EMPTY][:k]
+
+    def insert(self, batch, beam_width_construction: int = 200, alpha: float = 1.2) -> int:
+        """ComputeService::insert (src/service/compute_service.cc:152-196): `batch`
+        is a list of (id, values); returns the number inserted."""
+        if self.index is None:
+            raise DvsError(1, "no index loaded")
+        if not batch:
+            return 0
+        for _, values in batch:
+            if len(values) != self.dim:
+                raise ValueError("insert dimension mismatch")
+        ids = np.array([int(i) for i, _ in batch], np.uint32)
+        X = np.array([np.asarray(v, np.float32) for _, v in batch], np.float32)
+        st = self.index.insert(X, ids, beam_width_construction=beam_width_construction, alpha=alpha)
+        return int(st["inserted"])
 
     def search_batch(self, queries, k: int | None = None):
         if self.index is None:

@@ -237,6 +237,61 @@ typedef struct dvs_write_params {
 dvs_status dvs_write_index(const dvs_write_params* p, const float* h_vecs, const uint32_t* h_adj,
                            const uint8_t* h_records, const float* h_rotation, const float* h_rotated_centroid);
 
+/* ---- online insert (Vamana::insert, src/vamana/vamana.hh:458-999) ----------- */
+
+/* An empty, replicated index on the given devices, for a service that starts
+ * without an offline build: inserts then grow it, the first one becoming the
+ * medoid (vamana.hh:479-546).  The rotation P (dim*dim, column-major), the
+ * rotated centroid and t_const are the artifacts every vector is quantized
+ * with (rabitq_artifacts.cc:22-73). */
+typedef struct dvs_create_params {
+  uint32_t dim;
+  uint32_t R;                      /* max out-degree, <= 64 */
+  uint32_t rabitq_bits;            /* 1, 2, 4 or 8 */
+  dvs_metric metric;               /* the medoid seed distance (distance.hh:80-159) */
+  const float* rotation;
+  const float* rotated_centroid;
+  double t_const;
+  const int* devices;              /* NULL = {0, 1, ..., num_devices-1} */
+  uint32_t num_devices;            /* 0 = 1 */
+  uint64_t capacity;               /* rows reserved up front, 0 = 1024 */
+} dvs_create_params;
+
+dvs_status dvs_create(const dvs_create_params* params, dvs_index** out);
+
+/* Reserves device rows for `capacity` nodes (inserts grow the arrays by
+ * doubling when they run out). */
+dvs_status dvs_reserve(dvs_index* index, uint64_t capacity);
+
+typedef struct dvs_insert_params {
+  uint32_t beam_width_construction;  /* L_c, 0 = 200 (--beam-width-construction, configuration.hh:120) */
+  float alpha;                       /* RobustPrune alpha, 0 = 1.2 (--alpha, configuration.hh:126) */
+  uint32_t max_batch;                /* vectors per step, 0 = 1024 */
+} dvs_insert_params;
+
+typedef struct dvs_insert_stats {
+  uint64_t inserted;
+  uint64_t steps;        /* frozen-graph steps the batch was split into */
+  uint64_t expansions;   /* beam expansions of the insert searches */
+  uint64_t distances;    /* exact distances of the insert searches */
+  uint64_t full_prunes;  /* reverse edges that met a full list and re-pruned it */
+  float device_ms;       /* insert-search kernel time */
+} dvs_insert_stats;
+
+/* ComputeService::insert (src/service/compute_service.cc:152-196) into a
+ * replicated index (DVS_ERR_UNSUPPORTED when sharded): node ids h_ids[i]
+ * (NULL: the current node count + i).  The vectors are inserted in steps of
+ * min(max_batch, current node count) vectors; every vector of a step searches
+ * the graph as it stood when the step began (exact distances, beam capacity
+ * L_c), its final beam is pruned with RobustPrune (robust_prune_kernel), the
+ * vector is quantized by the GPU quantizer (rabitq_quantize_single_kernel),
+ * and reverse edges are added in insert order (append, or RobustPrune of a
+ * full list).  Steps of one vector reproduce the reference's sequential
+ * insert.  Waits for work in flight on the index's devices first and holds the
+ * index lock while it runs. */
+dvs_status dvs_insert(dvs_index* index, const float* h_vectors, const uint32_t* h_ids, uint32_t n, uint32_t dim,
+                      const dvs_insert_params* params, dvs_insert_stats* stats);
+
 /* ---- offline builder (GPU) ---------------------------------------------- */
 
 /* Builds an index from n vectors on one device and, when output_prefix is set,

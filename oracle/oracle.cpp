@@ -644,7 +644,8 @@ struct KnnOut {
 };
 
 // mode 0 = rabitq_gpu, 1 = exact_gpu (src/common/configuration.hh:128-130).
-KnnOut knn_one(const Index& ix, const float* q, uint32_t L, int mode, const float* qr_in, const float* f_in) {
+KnnOut knn_one(const Index& ix, const float* q, uint32_t L, int mode, const float* qr_in, const float* f_in,
+               bool sort_final = true) {
   KnnOut o;
   const bool rabitq = mode == 0;
   const uint32_t D = ix.dim;
@@ -706,8 +707,217 @@ KnnOut knn_one(const Index& ix, const float* q, uint32_t L, int mode, const floa
     for (auto& e : beam) e.distance = l2_ref(q, ix.vecs + size_t(e.id) * D, D);
     o.Cr = uint32_t(beam.size());
   }
-  std::sort(beam.begin(), beam.end(), [](const BeamEntry& a, const BeamEntry& b) { return a.distance < b.distance; });
+  if (sort_final)
+    std::sort(beam.begin(), beam.end(), [](const BeamEntry& a, const BeamEntry& b) { return a.distance < b.distance; });
   return o;
+}
+
+
+// ----------------------------------------------------------------------------
+// Online insert (src/vamana/vamana.hh:458-999)
+// ----------------------------------------------------------------------------
+
+// rabitq_quantize_single_kernel<4,B> (src/gpu/kernels/distance_kernels.cuh:376-464)
+// on an already rotated vector: float arithmetic, lane t of the 4-lane tile
+// takes dims j = t mod 4, tile sums by the butterfly, IEEE division and square
+// root, nvcc's contractions (every `acc += a*b` is an fma; the double
+// t_const*|o| + 1e-5 is a double fma).  The online insert quantizes with this
+// kernel, not with the offline builder's routine.
+void quantize_gpu_rotated(const float* r, const float* c, double tc, uint32_t dim, uint32_t bits, uint8_t* out) {
+  const uint32_t packed = (bits * dim + 7) / 8;
+  float l2p[4] = {0, 0, 0, 0};
+  for (uint32_t j = 0; j < dim; ++j) {
+    const float diff = r[j] - c[j];
+    l2p[j & 3] = std::fmaf(diff, diff, l2p[j & 3]);
+  }
+  const float l2_sqr = tile4(l2p);
+  const float l2_norm = std::sqrt(l2_sqr);
+  std::vector<uint8_t> u(dim);
+  float ipp[4] = {0, 0, 0, 0};
+  const int top = 1 << (bits - 1);
+  for (uint32_t j = 0; j < dim; ++j) {
+    const float abs_o = std::fabs((r[j] - c[j]) / l2_norm);
+    int val = static_cast<int>(std::fma(tc, static_cast<double>(abs_o), 1e-5));
+    if (val >= top) val = top - 1;
+    u[j] = static_cast<uint8_t>(val);
+    ipp[j & 3] = std::fmaf(static_cast<float>(val) + 0.5f, abs_o, ipp[j & 3]);
+  }
+  const float ip_norm = tile4(ipp);
+  const float ip_norm_inv = ip_norm == 0.0f ? 1.0f : 1.0f / ip_norm;
+  const uint32_t mask = uint32_t(top) - 1u;
+  for (uint32_t j = 0; j < dim; ++j) {
+    if (r[j] - c[j] >= 0.0f)
+      u[j] = static_cast<uint8_t>(u[j] + top);
+    else
+      u[j] = static_cast<uint8_t>((~u[j]) & mask);
+  }
+  const float cb = -(static_cast<float>(top) - 0.5f);
+  float rx[4] = {0, 0, 0, 0}, cx[4] = {0, 0, 0, 0};
+  for (uint32_t j = 0; j < dim; ++j) {
+    const float residual = r[j] - c[j];
+    const float xu_cb = static_cast<float>(u[j]) + cb;
+    rx[j & 3] = std::fmaf(residual, xu_cb, rx[j & 3]);
+    cx[j & 3] = std::fmaf(c[j], xu_cb, cx[j & 3]);
+  }
+  float ip_resi = tile4(rx);
+  const float ip_cent = tile4(cx);
+  if (ip_resi == 0.0f) ip_resi = std::numeric_limits<float>::max();
+  const float add = l2_sqr + ((2.0f * l2_sqr) * ip_cent) / ip_resi;
+  const float rescale = (ip_norm_inv * -2.0f) * l2_norm;
+  const uint32_t per = 8 / bits;
+  for (uint32_t b = 0; b < packed; ++b) {
+    uint32_t v = 0;
+    for (uint32_t k = 0; k < per && b * per + k < dim; ++k) v |= uint32_t(u[b * per + k]) << (k * bits);
+    out[b] = static_cast<uint8_t>(v);
+  }
+  std::memcpy(out + packed, &add, 4);
+  std::memcpy(out + packed + 4, &rescale, 4);
+}
+
+// robust_prune_kernel (src/gpu/kernels/distance_kernels.cuh:285-370): candidates
+// sorted by distance from the source (position s holds original index
+// order[s], or s); the nearest valid candidate is kept, and every later valid
+// candidate p' with alpha * |p* - p'|^2 <= d(source, p') is dropped (the
+// squared distance a sequential fma chain over the dims), until R are kept.
+// Writes original indices; returns the count.
+uint32_t robust_prune_gpu(const float* vecs, uint32_t vstride, const float* dists, const uint32_t* order, uint32_t n,
+                          uint32_t dim, float alpha, uint32_t R, uint32_t* out) {
+  if (n <= R) {
+    for (uint32_t i = 0; i < n; ++i) out[i] = order ? order[i] : i;
+    return n;
+  }
+  std::vector<char> valid(n, 1);
+  uint32_t cnt = 0;
+  for (uint32_t start = 0; start < n && cnt < R; ++start) {
+    if (!valid[start]) continue;
+    const uint32_t ps = order ? order[start] : start;
+    out[cnt++] = ps;
+    const float* pv = vecs + size_t(ps) * vstride;
+    for (uint32_t i = start + 1; i < n; ++i) {
+      if (!valid[i]) continue;
+      const float* qv = vecs + size_t(order ? order[i] : i) * vstride;
+      float d = 0.0f;
+      for (uint32_t k = 0; k < dim; ++k) {
+        const float diff = pv[k] - qv[k];
+        d = std::fmaf(diff, diff, d);
+      }
+      if (alpha * d <= dists[i]) valid[i] = 0;
+    }
+  }
+  return cnt;
+}
+
+// A mutable index with spare rows for inserts.
+struct MutIndex {
+  uint32_t n, cap, dim, R, bits, metric, medoid;
+  uint32_t* adj;
+  uint8_t* records;
+  uint32_t rec_size;
+  float* vecs;
+  uint32_t* ids;
+  const float* P;
+  const float* c_rot;
+  double tc;
+};
+
+// Appends slot `v`'s reverse edge to `nb` (vamana.hh:795-986): room -> append;
+// full -> RobustPrune of nb's neighbours plus v from nb's vector, distances by
+// batch_l2_squared_distance_kernel, ordered by (distance, position).
+void reverse_edge(MutIndex& ix, uint32_t nb, uint32_t v, float alpha) {
+  uint32_t* row = ix.adj + size_t(nb) * ix.R;
+  uint32_t cnt = 0;
+  while (cnt < ix.R && row[cnt] != kEmpty) ++cnt;
+  if (cnt < ix.R) {
+    row[cnt] = v;
+    return;
+  }
+  std::vector<uint32_t> all(row, row + ix.R);
+  all.push_back(v);
+  const uint32_t n_all = uint32_t(all.size());
+  const float* src = ix.vecs + size_t(nb) * ix.dim;
+  std::vector<float> d(n_all);
+  std::vector<float> cand(size_t(n_all) * ix.dim);
+  for (uint32_t i = 0; i < n_all; ++i) {
+    std::memcpy(&cand[size_t(i) * ix.dim], ix.vecs + size_t(all[i]) * ix.dim, size_t(ix.dim) * 4);
+    d[i] = l2_ref(src, &cand[size_t(i) * ix.dim], ix.dim);
+  }
+  std::vector<uint32_t> order(n_all);
+  for (uint32_t i = 0; i < n_all; ++i) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return d[a] < d[b]; });
+  std::vector<float> sd(n_all);
+  for (uint32_t i = 0; i < n_all; ++i) sd[i] = d[order[i]];
+  std::vector<uint32_t> kept(ix.R);
+  const uint32_t nk = robust_prune_gpu(cand.data(), ix.dim, sd.data(), order.data(), n_all, ix.dim, alpha, ix.R,
+                                       kept.data());
+  for (uint32_t i = 0; i < ix.R; ++i) row[i] = i < nk ? all[kept[i]] : kEmpty;
+}
+
+struct InsertCounts {
+  uint64_t H = 0, E = 0, full_prunes = 0;
+};
+
+// One batch: every vector searches the graph as it stood at the start of the
+// batch (beam search with exact distances, capacity L_c, vamana.hh:566-661),
+// its final beam in beam order is pruned (vamana.hh:663-746), the new nodes
+// are written, then reverse edges are added in insert order
+// (vamana.hh:795-986).  An empty index first takes vector 0 as the medoid
+// with no neighbours (vamana.hh:479-546).
+void insert_batch(MutIndex& ix, const float* X, const uint32_t* new_ids, uint32_t B, uint32_t Lc, float alpha,
+                  InsertCounts& cnt, int threads) {
+  const uint32_t D = ix.dim;
+  const uint32_t rs = ix.rec_size;
+  auto write_node = [&](uint32_t slot, const float* x, uint32_t id, const uint32_t* nbrs, uint32_t nn) {
+    std::memcpy(ix.vecs + size_t(slot) * D, x, size_t(D) * 4);
+    ix.ids[slot] = id;
+    std::vector<float> r(D);
+    rotate(ix.P, x, D, r.data());
+    quantize_gpu_rotated(r.data(), ix.c_rot, ix.tc, D, ix.bits, ix.records + size_t(slot) * rs);
+    uint32_t* row = ix.adj + size_t(slot) * ix.R;
+    for (uint32_t j = 0; j < ix.R; ++j) row[j] = j < nn ? nbrs[j] : kEmpty;
+  };
+  uint32_t first = 0;
+  if (ix.n == 0 && B > 0) {
+    write_node(0, X, new_ids[0], nullptr, 0);
+    ix.medoid = 0;
+    ix.n = 1;
+    first = 1;
+  }
+  const uint32_t m = B - first;
+  if (m == 0) return;
+  const uint32_t n0 = ix.n;
+  Index frozen{ix.n, D, ix.R, ix.bits, ix.metric, ix.medoid, ix.adj, ix.records, rs, ix.vecs, ix.P, ix.c_rot};
+  std::vector<uint32_t> pruned(size_t(m) * ix.R, kEmpty), npr(m);
+  std::vector<uint32_t> H(m), E(m);
+  parallel_for(0, m, threads, [&](size_t i) {
+    const KnnOut o = knn_one(frozen, X + size_t(first + i) * D, Lc, 1, nullptr, nullptr, false);
+    H[i] = o.H;
+    E[i] = o.E;
+    const uint32_t nc = uint32_t(o.beam.size());
+    std::vector<float> cv(size_t(nc) * D), cd(nc);
+    for (uint32_t c = 0; c < nc; ++c) {
+      std::memcpy(&cv[size_t(c) * D], ix.vecs + size_t(o.beam[c].id) * D, size_t(D) * 4);
+      cd[c] = o.beam[c].distance;
+    }
+    std::vector<uint32_t> kept(ix.R);
+    const uint32_t nk = robust_prune_gpu(cv.data(), D, cd.data(), nullptr, nc, D, alpha, ix.R, kept.data());
+    npr[i] = nk;
+    for (uint32_t j = 0; j < nk; ++j) pruned[size_t(i) * ix.R + j] = o.beam[kept[j]].id;
+  });
+  for (uint32_t i = 0; i < m; ++i) {
+    write_node(n0 + i, X + size_t(first + i) * D, new_ids[first + i], &pruned[size_t(i) * ix.R], npr[i]);
+    cnt.H += H[i];
+    cnt.E += E[i];
+  }
+  ix.n = n0 + m;
+  for (uint32_t i = 0; i < m; ++i)
+    for (uint32_t j = 0; j < npr[i]; ++j) {
+      const uint32_t nb = pruned[size_t(i) * ix.R + j];
+      uint32_t c = 0;
+      const uint32_t* row = ix.adj + size_t(nb) * ix.R;
+      while (c < ix.R && row[c] != kEmpty) ++c;
+      if (c == ix.R) ++cnt.full_prunes;
+      reverse_edge(ix, nb, n0 + i, alpha);
+    }
 }
 
 bool write_all(const std::string& path, const void* data, size_t bytes) {
@@ -942,6 +1152,38 @@ int orc_knn(uint32_t n, uint32_t dim, uint32_t R, uint32_t bits, uint32_t metric
       }
     }
   });
+  return 0;
+}
+
+
+// --- online insert ---
+void orc_quantize_gpu_rotated(const float* x_rot, const float* c_rot, double tc, uint32_t dim, uint32_t bits,
+                              uint8_t* out) {
+  quantize_gpu_rotated(x_rot, c_rot, tc, dim, bits, out);
+}
+
+uint32_t orc_robust_prune_gpu(const float* vecs, const float* dists, const uint32_t* order, uint32_t n, uint32_t dim,
+                              float alpha, uint32_t R, uint32_t* out) {
+  return robust_prune_gpu(vecs, dim, dists, order, n, dim, alpha, R, out);
+}
+
+// Inserts B vectors into an index held in caller arrays with room for `cap`
+// rows; *n and *medoid are updated.  counts = {expansions, distances, full prunes}.
+int orc_insert_batch(uint32_t* n, uint32_t cap, uint32_t dim, uint32_t R, uint32_t bits, uint32_t metric,
+                     uint32_t* medoid, uint32_t* adj, uint8_t* records, uint32_t rec_size, float* vecs, uint32_t* ids,
+                     const float* P, const float* c_rot, double t_const, const float* X, const uint32_t* new_ids,
+                     uint32_t B, uint32_t Lc, float alpha, uint64_t* counts, int threads) {
+  if (*n + uint64_t(B) > cap) return -1;
+  MutIndex ix{*n, cap, dim, R, bits, metric, *medoid, adj, records, rec_size, vecs, ids, P, c_rot, t_const};
+  InsertCounts c;
+  insert_batch(ix, X, new_ids, B, Lc, alpha, c, threads);
+  *n = ix.n;
+  *medoid = ix.medoid;
+  if (counts) {
+    counts[0] = c.H;
+    counts[1] = c.E;
+    counts[2] = c.full_prunes;
+  }
   return 0;
 }
 

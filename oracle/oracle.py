@@ -65,6 +65,10 @@ def lib():
             "orc_knn": (i32, [u32, u32, u32, u32, u32, u32, _u32p, _u8p, u32, _f32p, _f32p, _f32p, _f32p, u32,
                               u32, u32, i32, vp, vp, _u32p, _f32p, _u32p, vp, vp, u32, i32]),
             "orc_make_deterministic_vector": (None, [u32, u64, _f32p]),
+            "orc_quantize_gpu_rotated": (None, [_f32p, _f32p, f64, u32, u32, _u8p]),
+            "orc_robust_prune_gpu": (u32, [_f32p, _f32p, vp, u32, u32, f32, u32, _u32p]),
+            "orc_insert_batch": (i32, [C.POINTER(u32), u32, u32, u32, u32, u32, C.POINTER(u32), _u32p, _u8p, u32,
+                                       _f32p, _u32p, _f32p, _f32p, f64, _f32p, _u32p, u32, u32, f32, _u64p, i32]),
             "orc_cpu_beam_search_batch": (i32, [_f32p, u64, u32, _u32p, u32, u32, _f32p, u32, u32, u32, i32,
                                                 _u32p, vp]),
         }
@@ -256,10 +260,30 @@ def write_shards(prefix, X, adj, medoid, records, P, c_rot, tc, bits, num_memory
         raise OSError(f"orc_write_shards failed for {prefix}")
 
 
+def quantize_gpu_rotated(x_rot, c_rot, tc, bits):
+    """rabitq_quantize_single_kernel<4,B> (src/gpu/kernels/distance_kernels.cuh:376-464)
+    on a rotated vector: the online insert's quantizer."""
+    x_rot = _f32(x_rot)
+    out = np.empty(rabitq_size(x_rot.shape[0], bits), np.uint8)
+    lib().orc_quantize_gpu_rotated(x_rot, _f32(c_rot), float(tc), x_rot.shape[0], bits, out)
+    return out
+
+
+def robust_prune_gpu(cand_vecs, sorted_dists, alpha, R, order=None):
+    """robust_prune_kernel (src/gpu/kernels/distance_kernels.cuh:285-370): kept
+    original candidate indices, in selection order."""
+    V = _f32(cand_vecs)
+    n, d = V.shape
+    out = np.empty(max(R, 1), np.uint32)
+    o = None if order is None else np.ascontiguousarray(order, np.uint32)
+    cnt = lib().orc_robust_prune_gpu(V, _f32(sorted_dists), _ptr(o), n, d, np.float32(alpha), R, out)
+    return out[:cnt].copy()
+
+
 class OracleIndex:
     """SoA view of an index as the oracle reads it."""
 
-    def __init__(self, X, adj, medoid, records, P, c_rot, t_const, bits, metric="l2"):
+    def __init__(self, X, adj, medoid, records, P, c_rot, t_const, bits, metric="l2", ids=None):
         self.X = _f32(X)
         self.adj = np.ascontiguousarray(adj, np.uint32)
         self.medoid = int(medoid)
@@ -271,6 +295,53 @@ class OracleIndex:
         self.metric = metric
         self.n, self.dim = self.X.shape
         self.R = self.adj.shape[1]
+        self.ids = np.arange(self.n, dtype=np.uint32) if ids is None else np.ascontiguousarray(ids, np.uint32)
+
+    @classmethod
+    def empty(cls, dim, R, P, c_rot, t_const, bits, metric="l2"):
+        return cls(np.zeros((0, dim), np.float32), np.zeros((0, R), np.uint32), 0,
+                   np.zeros((0, rabitq_size(dim, bits)), np.uint8), P, c_rot, t_const, bits, metric)
+
+    def insert(self, X, ids=None, beam_width_construction=200, alpha=1.2, max_batch=1024, threads=0):
+        """Vamana::insert (src/vamana/vamana.hh:458-999) in steps of
+        min(max_batch, node count) vectors: every vector of a step searches the
+        graph as of the step's start, reverse edges in insert order.  Returns
+        (expansions, distances, full prunes, steps)."""
+        X = _f32(X).reshape(-1, self.dim)
+        ids = (np.arange(self.n, self.n + X.shape[0], dtype=np.uint32) if ids is None
+               else np.ascontiguousarray(ids, np.uint32))
+        tot = [0, 0, 0, 0]
+        pos = 0
+        while pos < X.shape[0]:
+            b = min(max_batch, max(self.n, 1), X.shape[0] - pos)
+            c = self.insert_step(X[pos:pos + b], ids[pos:pos + b], beam_width_construction, alpha, threads)
+            tot = [t + x for t, x in zip(tot, c + (1,))]
+            pos += b
+        return tuple(tot)
+
+    def insert_step(self, X, ids, beam_width_construction, alpha, threads=0):
+        """One step: orc_insert_batch."""
+        X = _f32(X).reshape(-1, self.dim)
+        B = X.shape[0]
+        new_ids = np.ascontiguousarray(ids, np.uint32)
+        cap = self.n + B
+        pad = lambda a, rows, fill: np.concatenate([a, np.full((rows,) + a.shape[1:], fill, a.dtype)])
+        self.X = pad(self.X, B, 0)
+        self.adj = pad(self.adj, B, EMPTY)
+        self.records = pad(self.records, B, 0)
+        self.ids = pad(self.ids, B, 0)
+        n = C.c_uint32(self.n)
+        med = C.c_uint32(self.medoid)
+        counts = np.zeros(3, np.uint64)
+        rc = lib().orc_insert_batch(C.byref(n), cap, self.dim, self.R, self.bits, 1 if self.metric == "ip" else 0,
+                                    C.byref(med), self.adj.reshape(-1), self.records.reshape(-1),
+                                    self.records.shape[1], self.X, self.ids, self.P, self.c_rot, self.t_const, X,
+                                    new_ids, B, beam_width_construction, np.float32(alpha), counts, threads)
+        if rc != 0:
+            raise ValueError("oracle insert rejected its arguments")
+        self.n = n.value
+        self.medoid = med.value
+        return tuple(int(c) for c in counts)
 
     def knn(self, queries, k, beam_width, mode="rabitq_gpu", q_rot=None, factors=None, beam_cap=0, threads=0):
         """Vamana::knn (src/vamana/vamana.hh:57-452) over a batch of queries.

@@ -62,4 +62,11 @@ int ref_quantize_single(const float* d_vector, const float* d_P, const float* d_
   return r;
 }
 
+int ref_robust_prune(const float* d_src, const float* d_cand, const float* d_dists, const uint32_t* d_order,
+                     uint32_t n, uint32_t dim, float alpha, uint32_t R, uint32_t* d_out, uint32_t* d_count) {
+  Ctx c;
+  gpu::launch_robust_prune(c.s, c.e, d_src, d_cand, d_dists, d_order, n, dim, alpha, R, d_out, d_count);
+  return c.done();
+}
+
 }  // extern "C"

@@ -126,6 +126,48 @@ def main(out_dir):
             outs.append(o.cpu().numpy())
         np.savez(os.path.join(out_dir, f"quantize_d{dim}_b8.npz"), kind="quantize", bits=8, x=X, P=P,
                  c_rot=c_rot, t_const=tc, out=np.stack(outs))
+    # online insert: the GPU quantizer kernel and RobustPrune.  The quantizer is
+    # driven through launch_rabitq_quantize_single with P = I, so cuBLAS's
+    # rotation returns the input exactly and the fixture records the kernel's
+    # own arithmetic on a known rotated vector.  That kernel stores its two
+    # float factors at byte offset (bits*dim+7)/8 of the output, which is only
+    # aligned when that offset is a multiple of 4: the other sizes make a
+    # misaligned store, so only aligned sizes are recorded.
+    lib.ref_robust_prune.argtypes = [vp, vp, vp, vp, u32, u32, C.c_float, u32, vp, vp]
+    rngi = np.random.default_rng(2026)
+    for bits, dim in [(4, 96), (4, 40), (8, 128), (2, 96), (1, 128)]:
+        assert ((bits * dim + 7) // 8) % 4 == 0
+        X = rngi.standard_normal((48, dim)).astype(np.float32)
+        c_rot = (0.1 * rngi.standard_normal(dim)).astype(np.float32)
+        eye = np.eye(dim, dtype=np.float32)
+        tc = O.t_const(dim, bits, 1234)
+        rs = O.rabitq_size(dim, bits)
+        outs = []
+        for x in X:
+            o = torch.zeros(rs, dtype=torch.uint8, device="cuda")
+            assert lib.ref_quantize_single(p(dev(x)), p(dev(eye)), p(dev(c_rot)), p(o), dim, bits, tc) == 0
+            outs.append(o.cpu().numpy())
+        np.savez(os.path.join(out_dir, f"quantize_gpu_d{dim}_b{bits}.npz"), kind="quantize_gpu", bits=bits,
+                 x_rot=X, c_rot=c_rot, t_const=tc, out=np.stack(outs))
+    for name, n, dim, R, alpha, permute in [("a", 120, 32, 16, 1.2, False), ("b", 120, 32, 16, 1.0, True),
+                                            ("c", 10, 24, 16, 1.2, False), ("d", 65, 96, 64, 1.2, True)]:
+        src = rngi.standard_normal(dim).astype(np.float32)
+        V = (src + 0.5 * rngi.standard_normal((n, dim))).astype(np.float32)
+        d = O.l2_batch(src, V)
+        order = np.argsort(d, kind="stable").astype(np.uint32)
+        if permute:
+            cand, dists, ordv = V, d[order], order          # vectors in original order, order maps rank -> index
+        else:
+            cand, dists, ordv = V[order], d[order], None    # vectors already sorted
+        out = torch.zeros(R, dtype=torch.int32, device="cuda")
+        cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+        d_ord = dev(ordv) if ordv is not None else None
+        assert lib.ref_robust_prune(p(dev(src)), p(dev(cand)), p(dev(dists)), p(d_ord) if d_ord is not None else None,
+                                    n, dim, alpha, R, p(out), p(cnt)) == 0
+        k = int(cnt.item())
+        np.savez(os.path.join(out_dir, f"prune_{name}.npz"), kind="prune", cand=cand, dists=dists,
+                 order=ordv if ordv is not None else np.zeros(0, np.uint32), alpha=np.float32(alpha), R=R,
+                 out=out.cpu().numpy()[:k].astype(np.uint32))
     print("golden fixtures written to", out_dir)
 
 

@@ -230,5 +230,38 @@ def test_golden_reference_kernels(oracle, name):
         assert (codes(rec) == codes(ref)).mean() > 0.98
         np.testing.assert_allclose(rec[:, packed:].copy().view(np.float32), ref[:, packed:].copy().view(np.float32),
                                    rtol=2e-3, atol=1e-6)
+    elif kind == "quantize_gpu":
+        # rabitq_quantize_single_kernel on a known rotated vector: bit for bit
+        for x, ref in zip(g["x_rot"], g["out"]):
+            got = oracle.quantize_gpu_rotated(x, g["c_rot"], float(g["t_const"]), int(g["bits"]))
+            np.testing.assert_array_equal(got, ref)
+    elif kind == "prune":
+        order = g["order"] if g["order"].size else None
+        got = oracle.robust_prune_gpu(g["cand"], g["dists"], float(g["alpha"]), int(g["R"]), order)
+        np.testing.assert_array_equal(got, g["out"])
     else:
         pytest.fail(f"unknown golden kind {kind}")
+
+
+def test_oracle_insert_graph_properties(oracle):
+    """Online insert restated (Vamana::insert, src/vamana/vamana.hh:458-999):
+    rows stay duplicate-free, self-free, non-empty-first and within R; steps
+    double from an empty index; inserted vectors are found again."""
+    X = normalized_gaussian(900, 20, 61)
+    P = oracle.rotation_matrix(20, 3)
+    c_rot = oracle.rotate(P, oracle.centroid(X))
+    idx = oracle.OracleIndex.empty(20, 10, P, c_rot, oracle.t_const(20, 4, 3), 4)
+    H, E, full, steps = idx.insert(X, beam_width_construction=32, alpha=1.2, max_batch=128)
+    assert idx.n == 900 and idx.medoid == 0
+    sched, n = [], 0
+    while n < 900:
+        sched.append(min(128, max(n, 1), 900 - n))
+        n += sched[-1]
+    assert sched[:9] == [1, 1, 2, 4, 8, 16, 32, 64, 128] and steps == len(sched) == 15
+    for i in range(idx.n):
+        row = idx.adj[i][idx.adj[i] != oracle.EMPTY]
+        assert len(row) <= 10 and i not in row and len(set(row.tolist())) == len(row)
+        assert (idx.adj[i][len(row):] == oracle.EMPTY).all()
+    assert full > 0
+    ids, _, _ = idx.knn(X[::9], 1, 32)
+    assert (ids[:, 0] == np.arange(0, 900, 9)).mean() > 0.95
