@@ -54,6 +54,12 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--cache", default=os.environ.get("DVS_BENCH_CACHE", "/tmp/dvs_b200_bench"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["search", "insert"], default="search",
+                    help="insert: online insert throughput into the base index (dvs_insert)")
+    ap.add_argument("--insert-count", type=int, default=100_000)
+    ap.add_argument("--insert-batch", type=int, default=4096)
+    ap.add_argument("--beam-width-construction", type=int, default=128)
+    ap.add_argument("--alpha", type=float, default=1.2)
     ap.add_argument("--placement", choices=["replicate", "shard"], default="replicate",
                     help="shard: one process over --gpus devices, the index split by slot (run without torchrun)")
     return ap.parse_args()
@@ -540,10 +546,80 @@ def run_sharded(args):
     print(json.dumps(line), flush=True)
 
 
+def run_insert(args):
+    """Online insert throughput (Vamana::insert, src/vamana/vamana.hh:458-999):
+    --insert-count new vectors of the workload's distribution go into the base
+    index through dvs_insert (host vectors in, steps of at most --insert-batch),
+    wall clock around each call; the oracle's CPU insert on a bounded sample of
+    the same stream is the baseline."""
+    import torch
+
+    import dvstor_b200 as D
+    from dvstor_b200 import datasets
+
+    dist = Dist("gloo")
+    wp = workload_params(args.workload, args.n)
+    prefix = ensure_index(args, wp, 0, dist)
+    torch.cuda.set_device(0)
+    ix = D.Index(prefix, devices=(0,))
+    n0 = int(ix.info.num_vectors)
+    B, Lc, total = args.insert_batch, args.beam_width_construction, args.insert_count
+    warm = args.warmup * B
+    Xn = datasets.queries_for(args.workload, warm + total, stream=9)
+    ids = np.arange(n0, n0 + warm + total, dtype=np.uint32)
+    ix.reserve(n0 + warm + total)
+    ix.insert(Xn[:warm], ids[:warm], beam_width_construction=Lc, alpha=args.alpha, max_batch=B)
+    torch.cuda.synchronize()
+    sampler = clocks_sampler(0)
+    t_wall0 = time.time()
+    stats = {"expansions": 0, "distances": 0, "full_prunes": 0, "steps": 0, "device_ms": 0.0}
+    t = time.perf_counter()
+    for s in range(warm, warm + total, B):
+        st = ix.insert(Xn[s:s + B], ids[s:s + B], beam_width_construction=Lc, alpha=args.alpha, max_batch=B)
+        for key in stats:
+            stats[key] += st[key]
+    el = time.perf_counter() - t
+    clocks = clocks_summary(sampler, t_wall0, time.time())
+    value = total / el
+    # the inserted vectors are found again (rank 0 = themselves)
+    probe = slice(warm, warm + min(total, 2000))
+    got, _ = ix.search(Xn[probe], 10, 64)
+    self_hit = float((got[:, 0] == ids[probe]).mean())
+    ix.close()
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+
+        orc = O.read_index(prefix)
+        cores = os.cpu_count() or 1
+        m = min(total, max(B, 2000))
+        t = time.perf_counter()
+        orc.insert(Xn[warm:warm + m], ids[warm:warm + m], beam_width_construction=Lc, alpha=args.alpha, max_batch=B,
+                   threads=cores)
+        cel = time.perf_counter() - t
+        cpu = {"value": m / cel, "unit": "inserts/s", "cores": cores, "kind": "port",
+               "sample": f"{m} inserts into the same base index, Vamana::insert restated (steps of {B}, searches "
+                         f"on {cores} threads, reverse edges sequential), {cel:.1f}s"}
+    line = {
+        "metric": f"inserts/sec (L_c={Lc}, alpha={args.alpha})", "value": value, "unit": "inserts/s",
+        "n_gpus": 1, "steps": stats["steps"], "warmup": args.warmup, "ms_per_step": 1e3 * el / max(stats["steps"], 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "n_base": n0, "dim": wp["dim"], "R": wp["R"], "rabitq_bits": 4,
+                   "inserted": total, "insert_batch": B, "beam_width_construction": Lc, "alpha": args.alpha},
+        "e2e": {"value": value, "unit": "inserts/s", "h2d_bytes_per_step": B * wp["dim"] * 4 + B * 4,
+                "d2h_bytes_per_step": B * wp["R"] * 4},
+        "insert_stats": stats, "self_hit_at_1": self_hit, "gpu_launches": 7 * stats["steps"],
+        "clocks": clocks, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "insert":
+        run_insert(args)
     elif args.placement == "shard":
         run_sharded(args)
     else:
