@@ -572,12 +572,13 @@ def run_insert(args):
     torch.cuda.synchronize()
     sampler = clocks_sampler(0)
     t_wall0 = time.time()
-    stats = {"expansions": 0, "distances": 0, "full_prunes": 0, "steps": 0, "device_ms": 0.0}
+    stats = {"expansions": 0, "distances": 0, "full_prunes": 0, "steps": 0, "device_ms": 0.0, "prune_ms": 0.0,
+             "reverse_ms": 0.0, "max_incoming": 0}
     t = time.perf_counter()
     for s in range(warm, warm + total, B):
         st = ix.insert(Xn[s:s + B], ids[s:s + B], beam_width_construction=Lc, alpha=args.alpha, max_batch=B)
         for key in stats:
-            stats[key] += st[key]
+            stats[key] = max(stats[key], st[key]) if key == "max_incoming" else stats[key] + st[key]
     el = time.perf_counter() - t
     clocks = clocks_summary(sampler, t_wall0, time.time())
     value = total / el

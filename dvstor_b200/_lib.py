@@ -78,7 +78,8 @@ class InsertParams(C.Structure):
 
 class InsertStats(C.Structure):
     _fields_ = [("inserted", C.c_uint64), ("steps", C.c_uint64), ("expansions", C.c_uint64),
-                ("distances", C.c_uint64), ("full_prunes", C.c_uint64), ("device_ms", C.c_float)]
+                ("distances", C.c_uint64), ("full_prunes", C.c_uint64), ("device_ms", C.c_float),
+                ("prune_ms", C.c_float), ("reverse_ms", C.c_float), ("max_incoming", C.c_uint32)]
 
 
 _lib = None

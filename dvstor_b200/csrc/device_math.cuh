@@ -32,7 +32,8 @@ __device__ __forceinline__ float small_u2f(uint32_t x) {
 
 // One lane's share of batch_l2_squared_distance_kernel<4>
 // (src/gpu/kernels/distance_kernels.cuh:38-81): lane t of the quad walks float4
-// chunks t, t+4, ... then tail dim n4*4+t.  `q` and `x` are 16-byte aligned.
+// chunks t, t+4, ... then tail dim n4*4+t.  `q` and `x` are 16-byte aligned;
+// `x` is global memory (read through the read-only data path).
 __device__ __forceinline__ float l2_quad_partial(const float* __restrict__ q, const float* __restrict__ x,
                                                  uint32_t dim, uint32_t t) {
   const uint32_t n4 = dim >> 2;

@@ -66,6 +66,15 @@ struct Device {
   uint32_t* work = nullptr;
   uint32_t* ovf = nullptr;
   size_t ovf_slots = 0;
+  // online insert scratch, kept between calls so a step allocates nothing:
+  // sort keys/values (in, out), run targets/counts/offsets, CUB temp storage,
+  // step counters, phase events
+  uint32_t* ins_buf = nullptr;
+  size_t ins_buf_words = 0;
+  void* ins_temp = nullptr;
+  size_t ins_temp_bytes = 0;
+  unsigned long long* ins_stats = nullptr;
+  cudaEvent_t ins_ev[4] = {nullptr, nullptr, nullptr, nullptr};
   // kernel timing ring: (before prepare, after prepare, after search)
   static constexpr size_t kRing = 4096;
   std::vector<cudaEvent_t> tev;
@@ -88,6 +97,13 @@ struct Device {
     dev_free(counters);
     dev_free(work);
     dev_free(ovf);
+    dev_free(ins_buf);
+    dev_free(ins_temp);
+    dev_free(ins_stats);
+    ins_buf_words = ins_temp_bytes = 0;
+    for (auto& e : ins_ev)
+      if (e) cudaEventDestroy(e);
+    for (auto& e : ins_ev) e = nullptr;
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
     for (cudaEvent_t e : tev) cudaEventDestroy(e);

@@ -28,6 +28,8 @@
 #include <cmath>
 #include <vector>
 
+#include <cub/cub.cuh>
+
 #include "device_math.cuh"
 #include "index_state.h"
 
@@ -36,10 +38,73 @@ using dvs::fail;
 namespace dvs {
 namespace {
 
+// |a - b|^2 as one sequential fma chain over dims 0..dim-1 (the order of
+// robust_prune_kernel's `dist += diff * diff`).  Rows are 16-byte aligned;
+// 32 dims are loaded per batch so a distance waits on memory dim/32 times.
+__device__ __forceinline__ float chain_l2(const float* __restrict__ a, const float* __restrict__ b, uint32_t dim) {
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  const uint32_t n4 = dim >> 2;
+  float d = 0.f;
+  uint32_t k4 = 0;
+  for (; k4 + 8 <= n4; k4 += 8) {
+    float4 x[8], y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[j] = a4[k4 + j];
+      y[j] = b4[k4 + j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float t = __fsub_rn(x[j].x, y[j].x);
+      d = __fmaf_rn(t, t, d);
+      t = __fsub_rn(x[j].y, y[j].y);
+      d = __fmaf_rn(t, t, d);
+      t = __fsub_rn(x[j].z, y[j].z);
+      d = __fmaf_rn(t, t, d);
+      t = __fsub_rn(x[j].w, y[j].w);
+      d = __fmaf_rn(t, t, d);
+    }
+  }
+  for (uint32_t k = k4 * 4; k < dim; ++k) {
+    const float t = __fsub_rn(a[k], b[k]);
+    d = __fmaf_rn(t, t, d);
+  }
+  return d;
+}
+
+// Lane t's share of batch_l2_squared_distance_kernel<4> (the order of
+// l2_quad_partial: float4 chunks t, t+4, ... then tail dim n4*4 + t, diff = q - x)
+// with plain loads, so x may be in shared memory.
+__device__ __forceinline__ float l2_quad_any(const float* q, const float* x, uint32_t dim, uint32_t t) {
+  const uint32_t n4 = dim >> 2;
+  const float4* q4 = reinterpret_cast<const float4*>(q);
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  float acc = 0.f;
+  for (uint32_t i = t; i < n4; i += 4) {
+    const float4 a = x4[i], b = q4[i];
+    float d = __fsub_rn(b.x, a.x);
+    acc = __fmaf_rn(d, d, acc);
+    d = __fsub_rn(b.y, a.y);
+    acc = __fmaf_rn(d, d, acc);
+    d = __fsub_rn(b.z, a.z);
+    acc = __fmaf_rn(d, d, acc);
+    d = __fsub_rn(b.w, a.w);
+    acc = __fmaf_rn(d, d, acc);
+  }
+  const uint32_t tail = (n4 << 2) + t;
+  if (tail < dim) {
+    const float d = __fsub_rn(q[tail], x[tail]);
+    acc = __fmaf_rn(d, d, acc);
+  }
+  return acc;
+}
+
 constexpr uint32_t kQuantPerBlock = 8;    // vectors per quantize block (one lane quad each)
 constexpr uint32_t kPruneThreads = 128;
 constexpr uint32_t kRevWarps = 4;         // warps (targets in flight) per reverse-edge block
 constexpr uint32_t kMaxAll = 65;          // R + 1 candidates of an overflow prune (R <= 64)
+constexpr size_t kStageBudget = 160 * 1024;  // shared memory for staged candidate vectors per block
 
 // rabitq_quantize_single_kernel<4,B> (src/gpu/kernels/distance_kernels.cuh:376-464)
 // on rotated rows: lane t of a quad takes dims j = t mod 4; tile sums by the
@@ -125,16 +190,19 @@ __global__ void __launch_bounds__(32) insert_quantize_kernel(const float* __rest
 // vector v: its final beam (slots by ascending distance, from the search) is
 // the candidate list; the nearest valid candidate is kept and every later
 // valid p' with alpha * |p* - p'|^2 <= d(v, p') is dropped, until R are kept.
-// The kept slots are the new node's adjacency row (row0 + v).
+// The kept slots are the new node's adjacency row (row0 + v).  STAGED: the
+// candidates' vectors are copied to shared memory once (when Lc rows fit), so
+// the greedy loop reads no global memory.
+template <bool STAGED>
 __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLayout ix, const uint32_t* __restrict__ cand,
                                                                      const float* __restrict__ cand_d,
                                                                      const uint32_t* __restrict__ counters, uint32_t Lc,
                                                                      float alpha, uint64_t row0,
                                                                      uint32_t* __restrict__ adj) {
   extern __shared__ __align__(16) float sm[];
-  const uint32_t v = blockIdx.x, tid = threadIdx.x, R = ix.R, dim = ix.dim;
-  float* ps = sm;                                      // p*'s vector
-  float* dd = ps + ix.vec_stride;                      // candidate distances
+  const uint32_t v = blockIdx.x, tid = threadIdx.x, R = ix.R, dim = ix.dim, vs = ix.vec_stride;
+  float* rows = sm;                                    // STAGED: Lc candidate vectors; else p*'s vector
+  float* dd = rows + (STAGED ? size_t(Lc) * vs : vs);  // candidate distances
   uint32_t* sl = reinterpret_cast<uint32_t*>(dd + Lc);  // candidate slots
   uint8_t* valid = reinterpret_cast<uint8_t*>(sl + Lc);
   const uint32_t n = counters[size_t(v) * 4 + 3] & 0xFFFFu;
@@ -149,23 +217,31 @@ __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLa
     for (uint32_t j = tid; j < R; j += blockDim.x) row[j] = j < n ? sl[j] : kEmptySlot;
     return;
   }
+  if (STAGED) {
+    const uint32_t c4 = vs >> 2, lane = tid & 31;
+    for (uint32_t r = tid >> 5; r < n; r += blockDim.x >> 5) {
+      const float4* src = reinterpret_cast<const float4*>(vec_row(ix, sl[r]));
+      float4* dst = reinterpret_cast<float4*>(rows + size_t(r) * vs);
+      for (uint32_t c = lane; c < c4; c += 32) dst[c] = src[c];
+    }
+    __syncthreads();
+  }
   uint32_t kept = 0;  // identical in every thread
   for (uint32_t s = 0; s < n && kept < R; ++s) {
     if (!valid[s]) continue;
     const uint32_t pslot = sl[s];
     if (tid == 0) row[kept] = pslot;
     ++kept;
-    const float* pv = vec_row(ix, pslot);
-    for (uint32_t k = tid; k < dim; k += blockDim.x) ps[k] = pv[k];
-    __syncthreads();
+    const float* pv = rows + size_t(s) * vs;
+    if (!STAGED) {
+      const float* g = vec_row(ix, pslot);
+      for (uint32_t k = tid; k < dim; k += blockDim.x) rows[k] = g[k];
+      pv = rows;
+      __syncthreads();
+    }
     for (uint32_t i = s + 1 + tid; i < n; i += blockDim.x) {
       if (!valid[i]) continue;
-      const float* qv = vec_row(ix, sl[i]);
-      float d = 0.f;
-      for (uint32_t k = 0; k < dim; ++k) {
-        const float diff = __fsub_rn(ps[k], qv[k]);
-        d = __fmaf_rn(diff, diff, d);
-      }
+      const float d = chain_l2(pv, STAGED ? rows + size_t(i) * vs : vec_row(ix, sl[i]), dim);
       if (__fmul_rn(alpha, d) <= dd[i]) valid[i] = 0;
     }
     __syncthreads();
@@ -183,24 +259,32 @@ struct RevWarp {
 };
 
 // Reverse edges (vamana.hh:795-986): warp w takes old node targets[w] and
-// applies the new slots srcs[offs[w] .. offs[w+1]) in insert order.  A list
-// with room gets the new slot appended; a full one is replaced by RobustPrune
-// of its R neighbours plus the new node, from the target's vector, with the
-// distances of batch_l2_squared_distance_kernel<4> ordered by (distance,
-// position).  `full` counts the overflow prunes.
+// applies the new slots srcs[offs[w] .. offs[w+1]) in insert order (*nruns
+// groups; a group keyed by the empty slot is skipped).  A list with room gets
+// the new slot appended; a full one is replaced by RobustPrune of its R
+// neighbours plus the new node, from the target's vector, with the distances
+// of batch_l2_squared_distance_kernel<4> ordered by (distance, position).
+// stats[2] counts the overflow prunes, stats[3] keeps the largest group.
+template <bool STAGED>
 __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const DevLayout ix, uint32_t* __restrict__ adj,
                                                                        const uint32_t* __restrict__ targets,
                                                                        const uint32_t* __restrict__ offs,
                                                                        const uint32_t* __restrict__ srcs,
-                                                                       uint32_t ntargets, float alpha,
-                                                                       uint32_t* __restrict__ full) {
+                                                                       const uint32_t* __restrict__ nruns, float alpha,
+                                                                       unsigned long long* __restrict__ stats) {
   __shared__ RevWarp ws[kRevWarps];
+  extern __shared__ __align__(16) float rows_all[];  // STAGED: R + 1 vectors per warp
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   RevWarp& W = ws[wib];
-  const uint32_t R = ix.R, dim = ix.dim;
-  for (uint32_t w = blockIdx.x * kRevWarps + wib; w < ntargets; w += gridDim.x * kRevWarps) {
+  const uint32_t R = ix.R, dim = ix.dim, vs = ix.vec_stride;
+  float* rows = rows_all + size_t(wib) * (R + 1) * vs;
+  const uint32_t wpb = blockDim.x >> 5;
+  const uint32_t ntargets = *nruns;
+  for (uint32_t w = blockIdx.x * wpb + wib; w < ntargets; w += gridDim.x * wpb) {
     const uint32_t tg = targets[w];
+    if (tg == kEmptySlot) continue;
     uint32_t* row = adj + size_t(tg) * R;
+    if (lane == 0) atomicMax(stats + 3, static_cast<unsigned long long>(offs[w + 1] - offs[w]));
     for (uint32_t e = offs[w]; e < offs[w + 1]; ++e) {
       const uint32_t v = srcs[e];
       const uint32_t a0 = lane < R ? row[lane] : kEmptySlot;
@@ -213,16 +297,30 @@ __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const Dev
         __syncwarp();
         continue;
       }
-      if (lane == 0) atomicAdd(full, 1u);
+      if (lane == 0) atomicAdd(stats + 2, 1ull);
       const uint32_t n_all = R + 1;
       if (lane < R) W.all[lane] = a0;
       if (lane + 32 < R) W.all[lane + 32] = a1;
       if (lane == 0) W.all[R] = v;
       __syncwarp();
+      if (STAGED) {
+        const uint32_t c4 = vs >> 2;
+        for (uint32_t r = 0; r < n_all; ++r) {
+          const float4* src = reinterpret_cast<const float4*>(vec_row(ix, W.all[r]));
+          float4* dst = reinterpret_cast<float4*>(rows + size_t(r) * vs);
+          for (uint32_t c = lane; c < c4; c += 32) dst[c] = src[c];
+        }
+        __syncwarp();
+      }
+      auto cand_row = [&](uint32_t i) -> const float* {
+        return STAGED ? rows + size_t(i) * vs : vec_row(ix, W.all[i]);
+      };
       const float* tv = vec_row(ix, tg);
       for (uint32_t i0 = 0; i0 < n_all; i0 += 8) {
         const uint32_t i = i0 + (lane >> 2);
-        const float part = i < n_all ? l2_quad_partial(tv, vec_row(ix, W.all[i]), dim, lane & 3) : 0.f;
+        const float part = i < n_all ? (STAGED ? l2_quad_any(tv, cand_row(i), dim, lane & 3)
+                                               : l2_quad_partial(tv, cand_row(i), dim, lane & 3))
+                                     : 0.f;
         const float tot = quad_butterfly(part);
         if (i < n_all && (lane & 3) == 0) W.d[i] = tot;
       }
@@ -242,15 +340,10 @@ __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const Dev
         const uint32_t pidx = W.order[s];
         if (lane == 0) W.kept[kept] = W.all[pidx];
         ++kept;
-        const float* pv = vec_row(ix, W.all[pidx]);
+        const float* pv = cand_row(pidx);
         for (uint32_t i = s + 1 + lane; i < n_all; i += 32) {
           if (!W.valid[i]) continue;
-          const float* qv = vec_row(ix, W.all[W.order[i]]);
-          float d = 0.f;
-          for (uint32_t k = 0; k < dim; ++k) {
-            const float diff = __fsub_rn(pv[k], qv[k]);
-            d = __fmaf_rn(diff, diff, d);
-          }
+          const float d = chain_l2(pv, cand_row(W.order[i]), dim);
           if (__fmul_rn(alpha, d) <= W.sd[i]) W.valid[i] = 0;
         }
         __syncwarp();
@@ -261,21 +354,64 @@ __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const Dev
   }
 }
 
+// (target, new slot) pairs of the step's new adjacency rows in insert order:
+// entry i*R + j is row i's j-th neighbour (empty slots keep the empty key).
+__global__ void edge_pairs_kernel(const uint32_t* __restrict__ rows, uint32_t m, uint32_t R, uint32_t n0,
+                                  uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+  const uint32_t e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= m) return;
+  keys[e] = rows[e];
+  vals[e] = n0 + e / R;
+}
+
+// Sums of the insert searches' counters (H, E) into stats[0], stats[1].
+__global__ void sum_counters_kernel(const uint32_t* __restrict__ counters, uint32_t b,
+                                    unsigned long long* __restrict__ stats) {
+  unsigned long long h = 0, e = 0;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < b; i += gridDim.x * blockDim.x) {
+    h += counters[size_t(i) * 4 + 0];
+    e += counters[size_t(i) * 4 + 1];
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    h += __shfl_xor_sync(0xFFFFFFFFu, h, o);
+    e += __shfl_xor_sync(0xFFFFFFFFu, e, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(stats + 0, h);
+    atomicAdd(stats + 1, e);
+  }
+}
+
 constexpr uint32_t kInsertDefaultLc = 200;   // --beam-width-construction default (configuration.hh:120)
 constexpr float kInsertDefaultAlpha = 1.2f;  // --alpha default (configuration.hh:126)
 constexpr uint32_t kInsertDefaultBatch = 1024;
 
-// Scratch of one insert step beyond the query scratch.
-struct InsertScratch {
-  uint32_t* csr = nullptr;  // targets | offsets | sources
-  size_t csr_words = 0;
-  uint32_t* full = nullptr;
-  void release() {
-    dev_free(csr);
-    dev_free(full);
-    csr_words = 0;
+// Scratch of the insert steps, kept on the device between calls (a step
+// allocates nothing once it has grown): m = b*R sort keys and values in and
+// out, run targets, counts and offsets, the run count, CUB's temp storage, the
+// step counters (H, E, full prunes, largest group) and four phase events.
+dvs_status ensure_insert_scratch(Device& d, uint32_t m) {
+  const size_t words = 7 * size_t(m) + 4;
+  if (words > d.ins_buf_words) {
+    dev_free(d.ins_buf);
+    DVS_CUDA(cudaMalloc(&d.ins_buf, words * 4));
+    d.ins_buf_words = words;
   }
-};
+  uint32_t* k = d.ins_buf;
+  size_t t1 = 0, t2 = 0, t3 = 0;
+  DVS_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, t1, k, k, k, k, int(m), 0, 32, d.stream));
+  DVS_CUDA(cub::DeviceRunLengthEncode::Encode(nullptr, t2, k, k, k, k, int(m), d.stream));
+  DVS_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, t3, k, k, int(m) + 1, d.stream));
+  const size_t temp = std::max({t1, t2, t3});
+  if (temp > d.ins_temp_bytes) {
+    dev_free(d.ins_temp);
+    DVS_CUDA(cudaMalloc(&d.ins_temp, temp));
+    d.ins_temp_bytes = temp;
+  }
+  for (auto& e : d.ins_ev)
+    if (!e) DVS_CUDA(cudaEventCreate(&e));
+  return DVS_OK;
+}
 
 // Quantizes rows already rotated in d.qrot (b of them) into records row0..row0+b-1.
 dvs_status quantize_rows(Device& d, uint32_t b, uint64_t row0, double tc) {
@@ -291,13 +427,14 @@ dvs_status quantize_rows(Device& d, uint32_t b, uint64_t row0, double tc) {
 }
 
 // One step of b vectors on one device (all b search the graph of the step's start).
-dvs_status insert_step(dvs_index* ix, Device& d, InsertScratch& sc, const float* hx, const uint32_t* hid, uint32_t b,
-                       uint32_t Lc, float alpha, dvs_insert_stats& st) {
+dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t* hid, uint32_t b, uint32_t Lc,
+                       float alpha, dvs_insert_stats& st) {
   DevLayout& L = d.lay;
   const uint32_t dim = L.dim, R = L.R;
   const double tc = ix->host.info.t_const;
   const uint64_t n0 = L.n;
   dvs_status r = ensure_scratch(d, b, Lc, true);
+  if (r == DVS_OK) r = ensure_insert_scratch(d, b * R);
   if (r != DVS_OK) return r;
   DVS_CUDA(cudaMemcpyAsync(d.queries, hx, size_t(b) * dim * 4, cudaMemcpyHostToDevice, d.stream));
   // the vectors, ids and records of the new rows
@@ -321,72 +458,78 @@ dvs_status insert_step(dvs_index* ix, Device& d, InsertScratch& sc, const float*
                 true);
   if (r != DVS_OK) return r;
   // 3. RobustPrune of each beam into the new adjacency rows
-  const size_t psmem = size_t(L.vec_stride) * 4 + size_t(Lc) * 9 + 16;
-  if (psmem > 48 * 1024)
-    DVS_CUDA(cudaFuncSetAttribute(insert_prune_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(psmem)));
-  insert_prune_kernel<<<b, kPruneThreads, psmem, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha, n0,
-                                                             d.adj);
+  DVS_CUDA(cudaEventRecord(d.ins_ev[0], d.stream));
+  const size_t pstaged = size_t(Lc) * L.vec_stride * 4 + size_t(Lc) * 9 + 16;
+  if (pstaged <= kStageBudget) {
+    if (pstaged > 48 * 1024)
+      DVS_CUDA(cudaFuncSetAttribute(insert_prune_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(pstaged)));
+    insert_prune_kernel<true><<<b, kPruneThreads, pstaged, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha,
+                                                                       n0, d.adj);
+  } else {
+    const size_t psmem = size_t(L.vec_stride) * 4 + size_t(Lc) * 9 + 16;
+    if (psmem > 48 * 1024)
+      DVS_CUDA(cudaFuncSetAttribute(insert_prune_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(psmem)));
+    insert_prune_kernel<false><<<b, kPruneThreads, psmem, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha,
+                                                                      n0, d.adj);
+  }
   DVS_CUDA(cudaGetLastError());
-  std::vector<uint32_t> rows(size_t(b) * R), cnt(size_t(b) * 4);
+  DVS_CUDA(cudaEventRecord(d.ins_ev[1], d.stream));
+  sum_counters_kernel<<<std::min<uint32_t>((b + 255) / 256, 64), 256, 0, d.stream>>>(d.counters, b, d.ins_stats);
+  DVS_CUDA(cudaGetLastError());
+  // 5. reverse edges: (target, new slot) pairs grouped by target on the device
+  //    with a stable radix sort (insert order kept inside a group)
+  const uint32_t m = b * R;
+  uint32_t* keys_in = d.ins_buf;
+  uint32_t* vals_in = keys_in + m;
+  uint32_t* keys_out = vals_in + m;
+  uint32_t* vals_out = keys_out + m;
+  uint32_t* run_tg = vals_out + m;
+  uint32_t* run_cnt = run_tg + m;        // m + 1 entries
+  uint32_t* run_off = run_cnt + m + 1;   // m + 1 entries
+  uint32_t* nruns = run_off + m + 1;
+  DVS_CUDA(cudaEventRecord(d.ins_ev[2], d.stream));
+  edge_pairs_kernel<<<(m + 255) / 256, 256, 0, d.stream>>>(d.adj + n0 * R, m, R, uint32_t(n0), keys_in, vals_in);
+  DVS_CUDA(cudaGetLastError());
+  size_t tb = d.ins_temp_bytes;
+  DVS_CUDA(cub::DeviceRadixSort::SortPairs(d.ins_temp, tb, keys_in, keys_out, vals_in, vals_out, int(m), 0, 32,
+                                           d.stream));
+  tb = d.ins_temp_bytes;
+  DVS_CUDA(cub::DeviceRunLengthEncode::Encode(d.ins_temp, tb, keys_out, run_tg, run_cnt, nruns, int(m), d.stream));
+  tb = d.ins_temp_bytes;
+  DVS_CUDA(cub::DeviceScan::ExclusiveSum(d.ins_temp, tb, run_cnt, run_off, int(m) + 1, d.stream));
+  const size_t per_warp = size_t(R + 1) * L.vec_stride * 4;
+  L.n = n0 + b;
+  if (per_warp <= kStageBudget) {
+    const uint32_t wpb = uint32_t(std::max<size_t>(1, std::min<size_t>(kRevWarps, kStageBudget / per_warp)));
+    const size_t smem = wpb * per_warp;
+    if (smem > 48 * 1024 - sizeof(RevWarp) * kRevWarps)
+      DVS_CUDA(cudaFuncSetAttribute(reverse_edges_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)));
+    const uint32_t blocks = std::min<uint32_t>((m + wpb - 1) / wpb, d.sm_count * 16);
+    reverse_edges_kernel<true><<<blocks, wpb * 32, smem, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns, alpha,
+                                                                     d.ins_stats);
+  } else {
+    const uint32_t blocks = std::min<uint32_t>((m + kRevWarps - 1) / kRevWarps, d.sm_count * 8);
+    reverse_edges_kernel<false><<<blocks, kRevWarps * 32, 0, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
+                                                                          alpha, d.ins_stats);
+  }
+  DVS_CUDA(cudaGetLastError());
+  DVS_CUDA(cudaEventRecord(d.ins_ev[3], d.stream));
   uint32_t work[4] = {0, 0, 0, 0};
-  DVS_CUDA(cudaMemcpyAsync(rows.data(), d.adj + n0 * R, rows.size() * 4, cudaMemcpyDeviceToHost, d.stream));
-  DVS_CUDA(cudaMemcpyAsync(cnt.data(), d.counters, cnt.size() * 4, cudaMemcpyDeviceToHost, d.stream));
   DVS_CUDA(cudaMemcpyAsync(work, d.work, 16, cudaMemcpyDeviceToHost, d.stream));
   DVS_CUDA(cudaStreamSynchronize(d.stream));
+  d.rows = L.n;
   float ms = 0.f;
   DVS_CUDA(cudaEventElapsedTime(&ms, d.ev0, d.ev1));
   st.device_ms += ms;
+  DVS_CUDA(cudaEventElapsedTime(&ms, d.ins_ev[0], d.ins_ev[1]));
+  st.prune_ms += ms;
+  DVS_CUDA(cudaEventElapsedTime(&ms, d.ins_ev[2], d.ins_ev[3]));
+  st.reverse_ms += ms;
   if (work[1] & kErrCapacity)
-    return fail(DVS_ERR_CAPACITY, "an insert's visited set exceeded its capacity; nothing of this step was linked");
-  for (uint32_t i = 0; i < b; ++i) {
-    st.expansions += cnt[size_t(i) * 4 + 0];
-    st.distances += cnt[size_t(i) * 4 + 1];
-  }
-  // 5. reverse edges, grouped by target in insert order
-  std::vector<std::pair<uint32_t, uint32_t>> pairs;  // (target, new slot)
-  pairs.reserve(rows.size());
-  for (uint32_t i = 0; i < b; ++i)
-    for (uint32_t j = 0; j < R && rows[size_t(i) * R + j] != kEmpty; ++j)
-      pairs.emplace_back(rows[size_t(i) * R + j], uint32_t(n0 + i));
-  std::stable_sort(pairs.begin(), pairs.end(),
-                   [](const std::pair<uint32_t, uint32_t>& x, const std::pair<uint32_t, uint32_t>& y) {
-                     return x.first < y.first;
-                   });
-  std::vector<uint32_t> targets, offs, srcs;
-  for (size_t e = 0; e < pairs.size(); ++e) {
-    if (e == 0 || pairs[e].first != pairs[e - 1].first) {
-      targets.push_back(pairs[e].first);
-      offs.push_back(uint32_t(e));
-    }
-    srcs.push_back(pairs[e].second);
-  }
-  offs.push_back(uint32_t(pairs.size()));
-  const uint32_t nt = uint32_t(targets.size());
-  L.n = n0 + b;
-  d.rows = L.n;
-  if (nt == 0) return DVS_OK;
-  const size_t words = targets.size() + offs.size() + srcs.size();
-  if (words > sc.csr_words) {
-    dev_free(sc.csr);
-    DVS_CUDA(cudaMalloc(&sc.csr, words * 2 * 4));
-    sc.csr_words = words * 2;
-  }
-  if (!sc.full) DVS_CUDA(cudaMalloc(&sc.full, 4));
-  std::vector<uint32_t> packed;
-  packed.reserve(words);
-  packed.insert(packed.end(), targets.begin(), targets.end());
-  packed.insert(packed.end(), offs.begin(), offs.end());
-  packed.insert(packed.end(), srcs.begin(), srcs.end());
-  DVS_CUDA(cudaMemcpyAsync(sc.csr, packed.data(), words * 4, cudaMemcpyHostToDevice, d.stream));
-  DVS_CUDA(cudaMemsetAsync(sc.full, 0, 4, d.stream));
-  const uint32_t blocks = std::min<uint32_t>((nt + kRevWarps - 1) / kRevWarps, d.sm_count * 8);
-  reverse_edges_kernel<<<blocks, kRevWarps * 32, 0, d.stream>>>(L, d.adj, sc.csr, sc.csr + nt, sc.csr + 2 * nt + 1,
-                                                                 nt, alpha, sc.full);
-  DVS_CUDA(cudaGetLastError());
-  uint32_t full = 0;
-  DVS_CUDA(cudaMemcpyAsync(&full, sc.full, 4, cudaMemcpyDeviceToHost, d.stream));
-  DVS_CUDA(cudaStreamSynchronize(d.stream));
-  st.full_prunes += full;
+    return fail(DVS_ERR_CAPACITY, "an insert's visited set exceeded its capacity; that vector's links are partial");
   return DVS_OK;
 }
 
@@ -477,19 +620,26 @@ dvs_status dvs_insert(dvs_index* ix, const float* h_vectors, const uint32_t* h_i
     DVS_CUDA(cudaDeviceSynchronize());  // searches in flight on any stream finish first
     dvs_status s = dvs::grow_rows(d, n_start + n);
     if (s != DVS_OK) return s;
-    dvs::InsertScratch sc;
+    if (!d.ins_stats) DVS_CUDA(cudaMalloc(&d.ins_stats, 4 * sizeof(unsigned long long)));
+    DVS_CUDA(cudaMemsetAsync(d.ins_stats, 0, 4 * sizeof(unsigned long long), d.stream));
     dvs_insert_stats dst{};
     uint32_t pos = 0;
     while (pos < n && s == DVS_OK) {
       const uint64_t cur = d.lay.n;
       const uint32_t b = uint32_t(std::min<uint64_t>({uint64_t(max_batch), std::max<uint64_t>(cur, 1),
                                                       uint64_t(n - pos)}));
-      s = dvs::insert_step(ix, d, sc, h_vectors + size_t(pos) * dim, ids.data() + pos, b, Lc, alpha, dst);
+      s = dvs::insert_step(ix, d, h_vectors + size_t(pos) * dim, ids.data() + pos, b, Lc, alpha, dst);
       pos += b;
       ++dst.steps;
     }
-    sc.release();
     if (s != DVS_OK) return s;
+    unsigned long long cs[4] = {0, 0, 0, 0};
+    DVS_CUDA(cudaMemcpyAsync(cs, d.ins_stats, sizeof(cs), cudaMemcpyDeviceToHost, d.stream));
+    DVS_CUDA(cudaStreamSynchronize(d.stream));
+    dst.expansions = cs[0];
+    dst.distances = cs[1];
+    dst.full_prunes = cs[2];
+    dst.max_incoming = uint32_t(cs[3]);
     dst.inserted = n;
     if (&d == &ix->devs[0]) st = dst;
   }

@@ -276,6 +276,9 @@ typedef struct dvs_insert_stats {
   uint64_t distances;    /* exact distances of the insert searches */
   uint64_t full_prunes;  /* reverse edges that met a full list and re-pruned it */
   float device_ms;       /* insert-search kernel time */
+  float prune_ms;        /* new-node RobustPrune kernel time */
+  float reverse_ms;      /* reverse-edge grouping and kernel time */
+  uint32_t max_incoming; /* most new nodes linking to one old node in a step */
 } dvs_insert_stats;
 
 /* ComputeService::insert (src/service/compute_service.cc:152-196) into a
