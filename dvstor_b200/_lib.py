@@ -30,7 +30,7 @@ EXPORTED = (
     "dvs_host_index_info", "dvs_host_index_arrays", "dvs_host_index_free", "dvs_write_index", "dvs_last_error",
     "dvs_status_string", "dvs_device_count", "dvs_build_index", "dvs_set_kernel_timing", "dvs_kernel_times",
     "dvs_search_device_noalloc", "dvs_set_rotation", "dvs_query_prepare_tc", "dvs_create", "dvs_reserve",
-    "dvs_insert",
+    "dvs_insert", "dvs_index_artifacts",
 )
 
 
@@ -114,9 +114,10 @@ def lib():
             "dvs_host_index_info": [vp, C.POINTER(IndexInfo)],
             "dvs_host_index_arrays": [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
                                       C.POINTER(vp)],
-            "dvs_write_index": [C.POINTER(WriteParams), vp, vp, vp, vp, vp],
+            "dvs_write_index": [C.POINTER(WriteParams), vp, vp, vp, vp, vp, vp],
             "dvs_create": [C.POINTER(CreateParams), C.POINTER(vp)],
             "dvs_reserve": [vp, u64],
+            "dvs_index_artifacts": [vp, vp, vp],
             "dvs_insert": [vp, vp, vp, u32, u32, C.POINTER(InsertParams), C.POINTER(InsertStats)],
         }
         for name, args in sigs.items():

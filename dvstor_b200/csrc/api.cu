@@ -420,6 +420,14 @@ dvs_status dvs_close(dvs_index* ix) {
   return DVS_OK;
 }
 
+dvs_status dvs_index_artifacts(const dvs_index* ix, float* h_rotation, float* h_rotated_centroid) {
+  if (!ix) return fail(DVS_ERR_ARG, "null index");
+  const size_t d = ix->host.info.dim;
+  if (h_rotation) std::memcpy(h_rotation, ix->host.rotation.data(), d * d * 4);
+  if (h_rotated_centroid) std::memcpy(h_rotated_centroid, ix->host.rotated_centroid.data(), d * 4);
+  return DVS_OK;
+}
+
 dvs_status dvs_index_get_info(const dvs_index* ix, dvs_index_info* out) {
   if (!ix || !out) return fail(DVS_ERR_ARG, "null argument");
   *out = ix->host.info;
@@ -534,8 +542,6 @@ dvs_status dvs_search(dvs_index* ix, const float* h_queries, uint32_t nq, uint32
   if (stats) *stats = dvs_stats{};
   if (nq == 0) return DVS_OK;
   if (!h_queries || !h_out_ids || !h_out_dist) return fail(DVS_ERR_ARG, "null buffer");
-  for (size_t i = 0; i < size_t(nq) * dim; ++i)
-    if (!std::isfinite(h_queries[i])) return fail(DVS_ERR_ARG, "query contains a non-finite value");
   std::lock_guard<std::mutex> g(ix->mu);
   const size_t nd = ix->devs.size();
   std::vector<dvs_status> st(nd, DVS_OK);
@@ -569,6 +575,8 @@ dvs_status dvs_search(dvs_index* ix, const float* h_queries, uint32_t nq, uint32
       }
       ps.overflow_queries = work[2];
       ps.device_ms = ms;
+      if (work[1] & dvs::kErrNonFinite)
+        return fail(DVS_ERR_ARG, "a query contains a non-finite value; its results are empty");
       if (work[1] & dvs::kErrCapacity)
         return fail(DVS_ERR_CAPACITY, "a query's visited set exceeded its capacity; its results are partial");
       if (work[1] & dvs::kErrHopLimit)

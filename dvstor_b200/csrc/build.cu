@@ -1023,7 +1023,7 @@ dvs_status dvs_build_index(const dvs_build_params* bp, const float* h_vecs, uint
   wp.alpha = bp->alpha;
   wp.metric = bp->metric;
   wp.t_const = tc;
-  return dvs_write_index(&wp, h_vecs, adj.data(), rec.data(), P.data(), c_rot.data());
+  return dvs_write_index(&wp, h_vecs, adj.data(), rec.data(), P.data(), c_rot.data(), nullptr);
 }
 
 }  // extern "C"

@@ -366,7 +366,8 @@ dvs_status dvs_host_index_arrays(const dvs_host_index* h, const uint32_t** adj, 
 void dvs_host_index_free(dvs_host_index* h) { delete h; }
 
 dvs_status dvs_write_index(const dvs_write_params* p, const float* h_vecs, const uint32_t* h_adj,
-                           const uint8_t* h_records, const float* h_rotation, const float* h_rotated_centroid) {
+                           const uint8_t* h_records, const float* h_rotation, const float* h_rotated_centroid,
+                           const uint32_t* h_ids) {
   if (!p || !p->index_prefix || !h_vecs || !h_adj || !h_records || !h_rotation || !h_rotated_centroid)
     return fail(DVS_ERR_ARG, "null argument");
   const uint64_t n = p->num_vectors;
@@ -395,7 +396,7 @@ dvs_status dvs_write_index(const dvs_write_params* p, const float* h_vecs, const
       uint8_t* node = buf.data() + 16 + k * aligned;
       const uint64_t header = (i == p->medoid) ? (uint64_t(1) << 16) : 0;  // HEADER_IS_MEDOID
       std::memcpy(node, &header, 8);
-      const uint32_t id = uint32_t(i);
+      const uint32_t id = h_ids ? h_ids[i] : uint32_t(i);
       std::memcpy(node + lay.off_id(), &id, 4);
       std::memcpy(node + lay.off_vector(), h_vecs + i * p->dim, size_t(p->dim) * 4);
       std::memcpy(node + lay.off_rabitq(), h_records + i * rs, rs);

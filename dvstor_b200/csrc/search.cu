@@ -354,10 +354,14 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
     if (qi >= a.nq) break;
 
     // ---- per-query set-up ----
+    bool finite = true;
     for (uint32_t j = lane; j < a.dim_pad; j += 32) {
-      qv[j] = j < dim ? a.queries[size_t(qi) * dim + j] : 0.f;
+      const float x = j < dim ? a.queries[size_t(qi) * dim + j] : 0.f;
+      finite &= isfinite(x);
+      qv[j] = x;
       qr[j] = rabitq ? a.qrot[size_t(qi) * ix.vec_stride + j] : 0.f;
     }
+    const bool nonfinite = !__all_sync(kFull, finite);
     float q_add = 0.f, q_k1 = 0.f;
     if (rabitq) {
       q_add = a.qfac[size_t(qi) * 4 + 0];
@@ -383,6 +387,10 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
     float* bdo = bdB;
     uint32_t* bio = biB;
     uint32_t nb = 1, hcount = 1, gcount = 0, H = 0, E = 0, err = 0, scan_from = 0;
+    if (nonfinite) {
+      nb = 0;  // nothing is selectable: the loop ends at once and every result slot is empty
+      err = kErrNonFinite;
+    }
     bool overflow = false;
     uint32_t pf_node = kEmptySlot, pf[NPL];
 

@@ -87,6 +87,7 @@ struct SearchShape {
 constexpr uint32_t kErrCapacity = 1u;
 constexpr uint32_t kErrHopLimit = 2u;
 constexpr uint32_t kErrTimeout = 4u;
+constexpr uint32_t kErrNonFinite = 8u;  // the query held a NaN or an infinity: no search, empty results
 
 // Words of shared memory one warp of the search kernel uses.
 __host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap) {

@@ -160,6 +160,14 @@ class Index:
                                       _lib.MODE[mode], ptr(d_out_ids), ptr(d_out_dist), ptr(d_counters), s))
         return d_out_ids, d_out_dist
 
+    def artifacts(self):
+        """(rotation P as loaded — dim*dim column-major, flattened —, rotated centroid)."""
+        d = self.info.dim
+        P = np.empty(d * d, np.float32)
+        c = np.empty(d, np.float32)
+        check(lib().dvs_index_artifacts(self._h, ptr(P), ptr(c)))
+        return P, c
+
     def download(self):
         """Device layout back on the host: adj (n,R), records (n,rabitq_size), vecs (n,dim), ids (n,)."""
         n, i = self.info.num_vectors, self.info
@@ -261,8 +269,10 @@ def load_host_index(prefix: str):
 
 
 def write_index(prefix: str, vecs, adj, records, rotation, rotated_centroid, medoid: int, t_const: float, bits: int,
-                num_memory_nodes: int = 1, beam_width: int = 128, alpha: float = 1.2, metric: str = "l2") -> None:
-    """dvs_write_index: the reference's shard/meta/rotation formats."""
+                num_memory_nodes: int = 1, beam_width: int = 128, alpha: float = 1.2, metric: str = "l2",
+                ids=None) -> None:
+    """dvs_write_index: the reference's shard/meta/rotation formats (node ids:
+    `ids`, or the slot numbers when None)."""
     vecs = np.ascontiguousarray(vecs, np.float32)
     adj = np.ascontiguousarray(adj, np.uint32)
     records = np.ascontiguousarray(records, np.uint8)
@@ -272,4 +282,8 @@ def write_index(prefix: str, vecs, adj, records, rotation, rotated_centroid, med
     os.makedirs(os.path.dirname(os.path.abspath(prefix)), exist_ok=True)
     p = _lib.WriteParams(str(prefix).encode(), n, d, adj.shape[1], bits, num_memory_nodes, medoid, beam_width, alpha,
                          _lib.METRIC[metric], t_const)
-    check(lib().dvs_write_index(C.byref(p), ptr(vecs), ptr(adj), ptr(records), ptr(P), ptr(c)))
+    idp = None if ids is None else np.ascontiguousarray(ids, np.uint32)
+    if idp is not None and idp.shape != (n,):
+        raise ValueError("ids must have one entry per vector")
+    check(lib().dvs_write_index(C.byref(p), ptr(vecs), ptr(adj), ptr(records), ptr(P), ptr(c),
+                                ptr(idp) if idp is not None else None))

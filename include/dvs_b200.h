@@ -109,6 +109,12 @@ dvs_status dvs_index_get_info(const dvs_index* index, dvs_index_info* out);
 dvs_status dvs_index_download(const dvs_index* index, uint32_t* h_adj, uint8_t* h_records, float* h_vecs,
                               uint32_t* h_ids);
 
+/* The RaBitQ artifacts every vector of the index is quantized with: the
+ * rotation P (dim*dim, column-major) and the rotated centroid (dim floats),
+ * as loaded from <prefix>.rotation.bin or given to dvs_create.  Either output
+ * may be NULL. */
+dvs_status dvs_index_artifacts(const dvs_index* index, float* h_rotation, float* h_rotated_centroid);
+
 /* ---- search -------------------------------------------------------------- */
 
 /* Batched search through host buffers: ComputeService<Distance>::search
@@ -126,7 +132,10 @@ dvs_status dvs_search(dvs_index* index, const float* h_queries, uint32_t nq, uin
 /* Same search on device-resident buffers of device `device_slot` (index into
  * the open params' device list), asynchronous on `stream`.  d_counters (may be
  * NULL) receives nq*4 uint32 per query: expansions H, estimates E, reranked
- * rows C_r, result count. */
+ * rows C_r, and result count | error bits << 16 (1: visited set over capacity,
+ * 2: expansion limit, 8: the query held a NaN or an infinity and was not
+ * searched — its result slots are empty).  dvs_search reports the same
+ * conditions as DVS_ERR_CAPACITY, DVS_ERR_HOP_LIMIT and DVS_ERR_ARG. */
 dvs_status dvs_search_device(dvs_index* index, uint32_t device_slot, const float* d_queries, uint32_t nq,
                              uint32_t dim, uint32_t k, uint32_t beam_width, dvs_mode mode, uint32_t* d_out_ids,
                              float* d_out_dist, uint32_t* d_counters, void* stream);
@@ -218,8 +227,9 @@ void dvs_host_index_free(dvs_host_index* h);
 
 /* Writes an index in the reference's offline formats (write_vamana_shards,
  * tools/vamana_offline_builder.cc:1136-1267): node i goes to shard i mod M at
- * offset 16 + (i div M)*align8(node_size), stored id = i.  adj: n*R slot
- * indices (0xFFFFFFFF = empty, non-empty entries first); records: n*rabitq_size. */
+ * offset 16 + (i div M)*align8(node_size), stored id = h_ids[i] (i when h_ids
+ * is NULL).  adj: n*R slot indices (0xFFFFFFFF = empty, non-empty entries
+ * first); records: n*rabitq_size. */
 typedef struct dvs_write_params {
   const char* index_prefix;
   uint64_t num_vectors;
@@ -235,7 +245,8 @@ typedef struct dvs_write_params {
 } dvs_write_params;
 
 dvs_status dvs_write_index(const dvs_write_params* p, const float* h_vecs, const uint32_t* h_adj,
-                           const uint8_t* h_records, const float* h_rotation, const float* h_rotated_centroid);
+                           const uint8_t* h_records, const float* h_rotation, const float* h_rotated_centroid,
+                           const uint32_t* h_ids);
 
 /* ---- online insert (Vamana::insert, src/vamana/vamana.hh:458-999) ----------- */
 

@@ -161,8 +161,24 @@ def test_argument_errors(gpu, cases):
             assert e.value.name == name
         bad = normalized_gaussian(2, 96, 1)
         bad[1, 3] = np.nan
-        with pytest.raises(gpu.DvsError):
+        with pytest.raises(gpu.DvsError, match="non-finite") as e:
             ix.search(bad, 10, 64)
+        assert e.value.name == "DVS_ERR_ARG"
+        # device path: the non-finite query is flagged in its counters and left
+        # empty; the finite one is searched as usual
+        import torch
+
+        bad[0, 5] = np.inf
+        good = normalized_gaussian(1, 96, 2)
+        dq = torch.from_numpy(np.concatenate([bad, good])).cuda()
+        cnt = torch.zeros((3, 4), dtype=torch.int32, device="cuda")
+        ids, d = ix.search_device(dq, 10, 64, d_counters=cnt)
+        torch.cuda.synchronize()
+        c = cnt.cpu().numpy().view(np.uint32)
+        assert ((c[:2, 3] >> 16) == 8).all() and (c[:2, :3] == 0).all()
+        assert (ids[:2].cpu().numpy().view(np.uint32) == gpu.EMPTY).all() and torch.isinf(d[:2]).all()
+        ref_ids, ref_d = ix.search(good, 10, 64)
+        np.testing.assert_array_equal(ids[2].cpu().numpy().view(np.uint32), ref_ids[0])
     with pytest.raises(gpu.DvsError) as e:
         gpu.Index(case.prefix, expect_dim=64)
     assert e.value.name == "DVS_ERR_DIM"
