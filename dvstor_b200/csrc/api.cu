@@ -154,11 +154,12 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, Launc
   s.cap = cap;
   s.cap_pad = (cap + 31) / 32 * 32;
   if (d.lay.n < (1u << 24)) {
-    // 16-bit entries, 8 per 16-byte bucket; at least 1024 buckets.  The entry
-    // limit follows slots_per_entry even where the bucket minimum is larger.
+    // 16-bit entries, 8 per 16-byte bucket; at least 2^(W-14) buckets for hash
+    // width W (20 bits below 2^20 nodes, else 24).  The entry limit follows
+    // slots_per_entry even where the bucket minimum is larger.
     const uint32_t spe = slots_per_entry ? slots_per_entry : kDefaultSlots16;
-    s.vt16 = 1;
-    s.hbuckets = std::max(1024u, (cap * spe + 7) / 8);
+    s.vt16 = d.lay.n < (1u << 20) ? 20u : 24u;
+    s.hbuckets = std::max(1u << (s.vt16 - 14), (cap * spe + 7) / 8);
     s.hcap = s.hbuckets * 4;
     s.hlimit = std::min(s.hbuckets * 8, cap * spe) / 10 * 9;
   } else {

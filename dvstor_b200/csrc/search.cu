@@ -107,17 +107,20 @@ __device__ __forceinline__ bool bucket_contains(const uint32_t* tab, uint32_t nb
 }
 
 // Compact visited table for indexes of fewer than 2^24 nodes: NB buckets of
-// eight 16-bit entries, two-choice placement.  An id is mixed by two 24-bit
-// bijections h1, h2; for hash k it may live in bucket hk mod NB as the entry
-// (k << 14) | (hk div NB).  (bucket, entry) determines hk and hence the id, so
-// membership is exact with half the bytes of a 32-bit table, and a lookup is
-// two independent 16-byte loads instead of a probe chain.  0xFFFF is empty
-// (entries use 15 bits; NB >= 1024 keeps hk div NB below 2^14).
-__device__ __forceinline__ uint32_t mix24(uint32_t x) {
-  x = (x * 0x9E3779u) & 0xFFFFFFu;
-  x ^= x >> 12;
-  x = (x * 0x85EBCBu) & 0xFFFFFFu;
-  x ^= x >> 11;
+// eight 16-bit entries, two-choice placement.  An id is mixed by two W-bit
+// bijections h1, h2 (W = 20 for indexes of fewer than 2^20 nodes, else 24);
+// for hash k it may live in bucket hk mod NB as the entry (k << 14) |
+// (hk div NB).  (bucket, entry) determines hk and hence the id, so membership
+// is exact with half the bytes of a 32-bit table, and a lookup is two
+// independent 16-byte loads instead of a probe chain.  0xFFFF is empty
+// (entries use 15 bits; NB >= 2^(W-14) keeps hk div NB below 2^14, so W = 20
+// lets the table shrink to what the beam needs).
+__device__ __forceinline__ uint32_t mixw(uint32_t x, uint32_t w) {
+  const uint32_t mask = (1u << w) - 1u, s = w >> 1;
+  x = (x * 0x9E3779u) & mask;  // odd multiplier: a bijection modulo 2^w
+  x ^= x >> s;
+  x = (x * 0x85EBCBu) & mask;
+  x ^= x >> (s - 1);
   return x;
 }
 
@@ -158,9 +161,11 @@ enum : uint32_t { kVisited = 0, kFresh = 1, kNoRoom = 2 };
 
 // Looks `id` up and, when absent and `may_insert`, inserts it.  Returns
 // kVisited, kFresh, or kNoRoom (absent and not insertable here).
-__device__ __forceinline__ uint32_t visit16(uint32_t* tab, uint32_t nb, float inv_nb, uint32_t id, bool may_insert) {
-  const Slot16 s1 = split16(mix24(id ^ 0x5A5A5Au), nb, inv_nb, 0);
-  const Slot16 s2 = split16(mix24(id ^ 0x3C3C3Cu), nb, inv_nb, 1);
+__device__ __forceinline__ uint32_t visit16(uint32_t* tab, uint32_t nb, float inv_nb, uint32_t id, bool may_insert,
+                                            uint32_t w) {
+  const uint32_t mask = (1u << w) - 1u;
+  const Slot16 s1 = split16(mixw(id ^ (0x5A5A5Au & mask), w), nb, inv_nb, 0);
+  const Slot16 s2 = split16(mixw(id ^ (0x3C3C3Cu & mask), w), nb, inv_nb, 1);
   unsigned short* t16 = reinterpret_cast<unsigned short*>(tab);
   for (int attempt = 0; attempt < 4; ++attempt) {
     const uint4 v1 = load_bucket(tab, s1.b), v2 = load_bucket(tab, s2.b);
@@ -320,11 +325,17 @@ __device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n,
   return lo;
 }
 
+// Register cap of a search_kernel instantiation.  R <= 32 with records held in
+// registers: 152, so that with the compact visited table 13 warps fit an SM
+// (65,536 registers / (152 x 32)); the others are bounded by shared memory or
+// need their registers, and keep up to 255.
+__host__ __device__ constexpr int search_max_regs(int npl, int rch) { return npl == 1 && rch > 0 ? 152 : 255; }
+
 // BITS: code width.  NPL: adjacency slots per lane (R <= 32 * NPL).  RCH: 16-byte
 // chunks of a RaBitQ record a lane holds in registers (0 = records too large:
 // they are loaded after the visited check instead).
 template <int BITS, int NPL, int RCH>
-__global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
+__global__ void __maxnreg__(search_max_regs(NPL, RCH)) search_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint32_t smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const DevLayout& ix = a.ix;
@@ -380,7 +391,7 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
       if (!a.vt16) htab[4 * hash_slot(ix.medoid, a.hcap >> 2)] = ix.medoid;
     }
     __syncwarp();
-    if (a.vt16 && lane == 0) visit16(htab, a.hbuckets, a.inv_hbuckets, ix.medoid, true);
+    if (a.vt16 && lane == 0) visit16(htab, a.hbuckets, a.inv_hbuckets, ix.medoid, true, a.vt16);
     __syncwarp();
     float* bd = bdA;
     uint32_t* bi = biA;
@@ -467,7 +478,7 @@ __global__ void __launch_bounds__(256, 1) search_kernel(const SearchArgs a) {
           if (!in_spill) {
             uint32_t r;
             if (a.vt16) {
-              r = visit16(htab, a.hbuckets, a.inv_hbuckets, id, may_insert);
+              r = visit16(htab, a.hbuckets, a.inv_hbuckets, id, may_insert, a.vt16);
             } else {
               r = may_insert ? (bucket_insert(htab, a.hcap >> 2, id) ? kFresh : kVisited)
                              : (bucket_contains(htab, a.hcap >> 2, id) ? kVisited : kNoRoom);

@@ -62,7 +62,7 @@ struct SearchArgs {
   uint32_t* ovf = nullptr;          // per warp slot visited overflow tables
   uint32_t ovf_cap = 0, ovf_limit = 0;
   uint32_t hcap = 0, hlimit = 0;    // shared-memory visited table: words, entry limit
-  uint32_t vt16 = 0;                // 1: compact 16-bit two-choice table (n < 2^24)
+  uint32_t vt16 = 0;                // compact 16-bit two-choice table: its hash width (20 or 24), 0 = 32-bit table
   uint32_t hbuckets = 0;            // its bucket count (8 entries each)
   float inv_hbuckets = 0.f;
   uint32_t cap_pad = 0, dim_pad = 0;

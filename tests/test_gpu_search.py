@@ -124,6 +124,26 @@ def test_repeat_runs_are_identical_and_batches_independent(gpu, cases):
     assert e[0].shape == (0, 10)
 
 
+def test_visited_table_hash_widths(gpu, oracle, tmp_path):
+    """Indexes of 2^20 nodes or more hash visited ids with 24-bit bijections
+    (a 1024-bucket minimum), smaller ones with 20-bit bijections (tables sized to
+    the beam): both exact, on an index just past 2^20 nodes and on a small one."""
+    from dvstor_b200.builder import build_index
+
+    n = (1 << 20) + 4096
+    X = normalized_gaussian(n, 8, 31)
+    prefix = str(tmp_path / "big" / "idx")
+    build_index(X, prefix, R=16, beam_width=24, device=0)
+    orc = oracle.read_index(prefix)
+    Q = normalized_gaussian(200, 8, 32)
+    with gpu.Index(prefix) as ix:
+        for mode, L in (("rabitq_gpu", 32), ("exact_gpu", 48)):
+            ids, d, st = ix.search(Q, 10, L, mode, stats=True)
+            o_ids, o_d, o_cnt, b_ids, b_d = orc.knn(Q, 10, L, mode, beam_cap=L + (64 if mode == "rabitq_gpu" else 0))
+            assert_results_match(ids, d, o_ids, o_d, b_ids, b_d)
+            assert st["estimates"] == int(o_cnt[:, 1].sum())
+
+
 def test_overflow_path_is_exact(gpu, oracle, cases):
     """Queries whose visited set spills from the shared-memory table to the
     global-memory table return the same results (spill forced by shrinking the
