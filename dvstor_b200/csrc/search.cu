@@ -326,10 +326,11 @@ __device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n,
 }
 
 // Register cap of a search_kernel instantiation.  R <= 32 with records held in
-// registers: 152, so that with the compact visited table 13 warps fit an SM
-// (65,536 registers / (152 x 32)); the others are bounded by shared memory or
-// need their registers, and keep up to 255.
-__host__ __device__ constexpr int search_max_regs(int npl, int rch) { return npl == 1 && rch > 0 ? 152 : 255; }
+// registers: 128, four warps per SM sub-partition (16,384 registers each), so
+// that shared memory (13 warps with the compact visited table at L = 64), not
+// registers, bounds the warps per SM; the others are bounded by shared memory
+// or need their registers, and keep up to 255.
+__host__ __device__ constexpr int search_max_regs(int npl, int rch) { return npl == 1 && rch > 0 ? 128 : 255; }
 
 // BITS: code width.  NPL: adjacency slots per lane (R <= 32 * NPL).  RCH: 16-byte
 // chunks of a RaBitQ record a lane holds in registers (0 = records too large:
