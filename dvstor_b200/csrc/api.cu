@@ -167,7 +167,7 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, Launc
     s.hcap = std::max(64u, (cap * spe + 31) / 32 * 32);
     s.hlimit = s.hcap / 10 * 9;
   }
-  const uint32_t words = search_warp_words(s.cap_pad, d.lay.vec_stride, s.hcap);
+  const uint32_t words = search_warp_words(s.cap_pad, d.lay.vec_stride, s.hcap, d.lay.R);
   int best_warps = 0;
   for (uint32_t wpb : {1u, 2u, 4u, 8u}) {
     const size_t smem = size_t(wpb) * words * 4;

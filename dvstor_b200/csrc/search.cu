@@ -340,7 +340,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH)) search_kernel(const Searc
   extern __shared__ __align__(16) uint32_t smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const DevLayout& ix = a.ix;
-  uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap);
+  uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R);
   float* bdA = reinterpret_cast<float*>(base);
   uint32_t* biA = base + a.cap_pad;
   float* bdB = reinterpret_cast<float*>(base + 2 * a.cap_pad);
@@ -348,10 +348,10 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH)) search_kernel(const Searc
   float* qv = reinterpret_cast<float*>(base + 4 * a.cap_pad);
   float* qr = qv + a.dim_pad;
   uint32_t* cid = base + 4 * a.cap_pad + 2 * a.dim_pad;
-  float* cd = reinterpret_cast<float*>(cid + 64);
-  float* sd = reinterpret_cast<float*>(cid + 128);
-  uint32_t* sid = cid + 192;
-  uint32_t* htab = cid + 256;
+  float* cd = reinterpret_cast<float*>(cid + 32 * NPL);
+  float* sd = reinterpret_cast<float*>(cid + 64 * NPL);
+  uint32_t* sid = cid + 96 * NPL;
+  uint32_t* htab = cid + 128 * NPL;
   const uint32_t warp_slot = blockIdx.x * (blockDim.x >> 5) + wib;
   uint32_t* gtab = a.ovf ? a.ovf + size_t(warp_slot) * a.ovf_cap : nullptr;
   const bool rabitq = a.mode == 0;
@@ -584,6 +584,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH)) search_kernel(const Searc
         rank[h] = 0;
         ins[h] = i < ms ? lower_bound_smem(bd, nb, nd[h]) : 0xFFFFFFFFu;
       }
+#pragma unroll 4
       for (uint32_t j = 0; j < ms; ++j) {
         const float dj = __shfl_sync(kFull, nd[j >> 5], j & 31);
 #pragma unroll
@@ -606,10 +607,27 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH)) search_kernel(const Searc
         }
       }
       first_pos = __reduce_min_sync(kFull, first_pos);
+      // beam entry p moves down by #{survivors with ins <= p}.  ins depends on
+      // the distance alone, so in rank order it never decreases: the count is
+      // an upper-bound search of the insertion points laid out by rank (in sd,
+      // whose distances were read into nd above).
+      uint32_t* sins = reinterpret_cast<uint32_t*>(sd);
+      __syncwarp();
+#pragma unroll
+      for (int h = 0; h < NPL; ++h)
+        if (32u * h + lane < ms) sins[rank[h]] = ins[h];
+      __syncwarp();
       for (uint32_t p0 = 0; p0 < nb; p0 += 32) {
         const uint32_t p = p0 + lane;
-        uint32_t shift = 0;
-        for (uint32_t j = 0; j < ms; ++j) shift += __shfl_sync(kFull, ins[j >> 5], j & 31) <= p;
+        uint32_t lo = 0, hi = ms;
+        while (lo < hi) {
+          const uint32_t mid = (lo + hi) >> 1;
+          if (sins[mid] <= p)
+            lo = mid + 1;
+          else
+            hi = mid;
+        }
+        const uint32_t shift = lo;
         if (p < nb && p + shift < a.cap) {
           bdo[p + shift] = bd[p];
           bio[p + shift] = bi[p];
@@ -785,7 +803,7 @@ cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, uin
 }
 
 cudaError_t launch_search(const SearchArgs& a, uint32_t wpb, uint32_t blocks, cudaStream_t stream) {
-  const size_t smem = size_t(wpb) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap) * 4;
+  const size_t smem = size_t(wpb) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, a.ix.R) * 4;
   const bool two = a.ix.R > 32;
   const int rch = record_chunks(a.ix.code_words);
   const dim3 grid(blocks), block(wpb * 32);

@@ -89,9 +89,12 @@ constexpr uint32_t kErrHopLimit = 2u;
 constexpr uint32_t kErrTimeout = 4u;
 constexpr uint32_t kErrNonFinite = 8u;  // the query held a NaN or an infinity: no search, empty results
 
-// Words of shared memory one warp of the search kernel uses.
-__host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap) {
-  return 4 * cap_pad + 2 * dim_pad + 256 + hcap;
+// Words of shared memory one warp of the search kernel uses: two beams (cap_pad
+// distances + ids each), query and rotated query, four candidate staging arrays
+// of 32 x slots-per-lane entries (slots per lane = 2 when R > 32, else 1), the
+// visited table.
+__host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R) {
+  return 4 * cap_pad + 2 * dim_pad + (R > 32 ? 256 : 128) + hcap;
 }
 
 // q' = P^T q (the sequential fmaf chain over i per output) and the query
