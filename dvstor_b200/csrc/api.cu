@@ -150,7 +150,7 @@ dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path) {
   return DVS_OK;
 }
 
-dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, LaunchShape& s) {
+dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool exact, LaunchShape& s) {
   s.cap = cap;
   s.cap_pad = (cap + 31) / 32 * 32;
   if (d.lay.n < (1u << 24)) {
@@ -173,7 +173,7 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, Launc
     const size_t smem = size_t(wpb) * words * 4;
     if (smem > 227 * 1024) break;
     int bps = 0;
-    const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, wpb, smem, &bps);
+    const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, exact, wpb, smem, &bps);
     if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
     if (int(wpb) * bps > best_warps) {
       best_warps = int(wpb) * bps;
@@ -185,7 +185,8 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, Launc
     return fail(DVS_ERR_CAPACITY, "beam capacity " + std::to_string(cap) + " needs more shared memory than a block has");
   // set the attribute for the chosen configuration last
   int bps = 0;
-  const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, s.wpb, size_t(s.wpb) * words * 4, &bps);
+  const cudaError_t e =
+      search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, exact, s.wpb, size_t(s.wpb) * words * 4, &bps);
   if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
   return DVS_OK;
 }
@@ -214,7 +215,7 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
   }
   const uint32_t cap = rabitq ? L + kBeamSlack : L;
   LaunchShape s;
-  dvs_status rc = launch_shape(d, cap, ix->slots_per_entry, s);
+  dvs_status rc = launch_shape(d, cap, ix->slots_per_entry, !rabitq, s);
   if (rc != DVS_OK) return rc;
   rc = ensure_scratch(d, nq, k, false);
   if (rc != DVS_OK) return rc;
@@ -678,10 +679,10 @@ dvs_status device_view(dvs_index* ix, uint32_t slot, DeviceView* out) {
   return DVS_OK;
 }
 
-dvs_status search_shape(dvs_index* ix, uint32_t slot, uint32_t cap, SearchShape* out) {
+dvs_status search_shape(dvs_index* ix, uint32_t slot, uint32_t cap, bool exact, SearchShape* out) {
   if (!ix || !out || slot >= ix->devs.size()) return fail(DVS_ERR_ARG, "bad argument");
   LaunchShape s;
-  const dvs_status rc = launch_shape(ix->devs[slot], cap, ix->slots_per_entry, s);
+  const dvs_status rc = launch_shape(ix->devs[slot], cap, ix->slots_per_entry, exact, s);
   if (rc != DVS_OK) return rc;
   out->cap = s.cap;
   out->cap_pad = s.cap_pad;

@@ -119,8 +119,8 @@ struct LaunchShape {
   uint32_t vt16 = 0, hbuckets = 0, hlimit = 0;
 };
 
-// Search-kernel launch shape for beam capacity `cap` on device `d`.
-dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, LaunchShape& s);
+// Search-kernel launch shape for beam capacity `cap` on device `d` (exact: exact_gpu mode).
+dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool exact, LaunchShape& s);
 // Grows the device's query scratch to nq queries (and nq*k results for host calls).
 dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path);
 // Prepare + search for nq device-resident queries on one device (asynchronous on st).

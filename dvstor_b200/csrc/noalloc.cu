@@ -104,7 +104,7 @@ extern "C" dvs_status dvs_search_device_noalloc(dvs_index* index, uint32_t devic
   if (s != DVS_OK) return s;
   const uint32_t cap = rabitq ? beam_width + kBeamSlack : beam_width;
   SearchShape sh;
-  s = search_shape(index, device_slot, cap, &sh);
+  s = search_shape(index, device_slot, cap, !rabitq, &sh);
   if (s != DVS_OK) return s;
 
   // layout of the fixed scratch: work words | factors | rotated queries | spill tables

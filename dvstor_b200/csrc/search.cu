@@ -330,13 +330,16 @@ __device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n,
 // that shared memory (13 warps with the compact visited table at L = 64), not
 // registers, bounds the warps per SM; the others are bounded by shared memory
 // or need their registers, and keep up to 255.
-__host__ __device__ constexpr int search_max_regs(int npl, int rch) { return npl == 1 && rch > 0 ? 128 : 255; }
+__host__ __device__ constexpr int search_max_regs(int npl, int rch, bool exact) {
+  return npl == 1 && (rch > 0 || exact) ? 128 : 255;
+}
 
-// BITS: code width.  NPL: adjacency slots per lane (R <= 32 * NPL).  RCH: 16-byte
+// EXACT: exact_gpu (exact distances, no records; BITS and RCH unused) or
+// rabitq_gpu.  BITS: code width.  NPL: adjacency slots per lane (R <= 32 * NPL).  RCH: 16-byte
 // chunks of a RaBitQ record a lane holds in registers (0 = records too large:
 // they are loaded after the visited check instead).
-template <int BITS, int NPL, int RCH>
-__global__ void __maxnreg__(search_max_regs(NPL, RCH)) search_kernel(const SearchArgs a) {
+template <int BITS, int NPL, int RCH, bool EXACT>
+__global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint32_t smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const DevLayout& ix = a.ix;
@@ -354,7 +357,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH)) search_kernel(const Searc
   uint32_t* htab = cid + 128 * NPL;
   const uint32_t warp_slot = blockIdx.x * (blockDim.x >> 5) + wib;
   uint32_t* gtab = a.ovf ? a.ovf + size_t(warp_slot) * a.ovf_cap : nullptr;
-  const bool rabitq = a.mode == 0;
+  constexpr bool rabitq = !EXACT;  // the mode is a template parameter: each kernel holds one loop body
   const uint32_t dim = ix.dim, R = ix.R;
   const uint32_t nch = (ix.code_words + 2 + 3) >> 2;
   const float kInf = __int_as_float(0x7F800000);
@@ -752,17 +755,18 @@ __global__ void l2_rows_kernel(const float* __restrict__ q, const float* __restr
   if (row < n && t == 0) out[row] = acc;
 }
 
-template <int BITS, int NPL, int RCH>
+template <int BITS, int NPL, int RCH, bool EXACT>
 cudaError_t occ(uint32_t wpb, size_t smem, int* bps) {
-  cudaError_t e = cudaFuncSetAttribute(search_kernel<BITS, NPL, RCH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(smem));
+  cudaError_t e = cudaFuncSetAttribute(search_kernel<BITS, NPL, RCH, EXACT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(bps, search_kernel<BITS, NPL, RCH>, int(wpb * 32), smem);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(bps, search_kernel<BITS, NPL, RCH, EXACT>, int(wpb * 32),
+                                                       smem);
 }
 
-template <int BITS, int NPL, int RCH>
+template <int BITS, int NPL, int RCH, bool EXACT>
 void launch(const SearchArgs& a, dim3 grid, dim3 block, size_t smem, cudaStream_t st) {
-  search_kernel<BITS, NPL, RCH><<<grid, block, smem, st>>>(a);
+  search_kernel<BITS, NPL, RCH, EXACT><<<grid, block, smem, st>>>(a);
 }
 
 // Record chunks a lane keeps in registers: 4 (<= 64-byte records) or 8
@@ -774,24 +778,27 @@ inline int record_chunks(uint32_t code_words) {
 
 template <int BITS, int NPL>
 cudaError_t occ_rch(int rch, uint32_t wpb, size_t smem, int* bps) {
-  return rch == 4 ? occ<BITS, NPL, 4>(wpb, smem, bps) : rch == 8 ? occ<BITS, NPL, 8>(wpb, smem, bps)
-                                                            : occ<BITS, NPL, 0>(wpb, smem, bps);
+  return rch == 4 ? occ<BITS, NPL, 4, false>(wpb, smem, bps)
+         : rch == 8 ? occ<BITS, NPL, 8, false>(wpb, smem, bps)
+                    : occ<BITS, NPL, 0, false>(wpb, smem, bps);
 }
 
 template <int BITS, int NPL>
 void launch_rch(int rch, const SearchArgs& a, dim3 g, dim3 b, size_t smem, cudaStream_t st) {
   if (rch == 4)
-    launch<BITS, NPL, 4>(a, g, b, smem, st);
+    launch<BITS, NPL, 4, false>(a, g, b, smem, st);
   else if (rch == 8)
-    launch<BITS, NPL, 8>(a, g, b, smem, st);
+    launch<BITS, NPL, 8, false>(a, g, b, smem, st);
   else
-    launch<BITS, NPL, 0>(a, g, b, smem, st);
+    launch<BITS, NPL, 0, false>(a, g, b, smem, st);
 }
 
 }  // namespace
 
-cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, uint32_t wpb, size_t smem, int* bps) {
+cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, bool exact, uint32_t wpb, size_t smem,
+                             int* bps) {
   const bool two = R > 32;
+  if (exact) return two ? occ<1, 2, 0, true>(wpb, smem, bps) : occ<1, 1, 0, true>(wpb, smem, bps);
   const int rch = record_chunks(code_words);
   switch (bits) {
     case 1: return two ? occ_rch<1, 2>(rch, wpb, smem, bps) : occ_rch<1, 1>(rch, wpb, smem, bps);
@@ -807,6 +814,10 @@ cudaError_t launch_search(const SearchArgs& a, uint32_t wpb, uint32_t blocks, cu
   const bool two = a.ix.R > 32;
   const int rch = record_chunks(a.ix.code_words);
   const dim3 grid(blocks), block(wpb * 32);
+  if (a.mode == 1) {
+    two ? launch<1, 2, 0, true>(a, grid, block, smem, stream) : launch<1, 1, 0, true>(a, grid, block, smem, stream);
+    return cudaGetLastError();
+  }
   switch (a.ix.bits) {
     case 1:
       two ? launch_rch<1, 2>(rch, a, grid, block, smem, stream) : launch_rch<1, 1>(rch, a, grid, block, smem, stream);

@@ -119,15 +119,15 @@ cudaError_t launch_search(const SearchArgs& a, uint32_t warps_per_block, uint32_
 
 // Occupancy helper: blocks per SM for `warps_per_block` warps with the given
 // per-warp shared memory; also sets the kernel's dynamic smem attribute.
-cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, uint32_t warps_per_block, size_t smem_bytes,
-                             int* blocks_per_sm);
+cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, bool exact, uint32_t warps_per_block,
+                             size_t smem_bytes, int* blocks_per_sm);
 
 }  // namespace dvs
 
 struct dvs_index;
 namespace dvs {
 dvs_status device_view(dvs_index* ix, uint32_t slot, DeviceView* out);
-dvs_status search_shape(dvs_index* ix, uint32_t slot, uint32_t cap, SearchShape* out);
+dvs_status search_shape(dvs_index* ix, uint32_t slot, uint32_t cap, bool exact, SearchShape* out);
 
 cudaError_t launch_estimate_ref_layout(const float* qrot, const float* f3, const uint8_t* records, float* out,
                                        uint32_t n, uint32_t dim, uint32_t bits, cudaStream_t stream);

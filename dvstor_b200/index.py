@@ -155,7 +155,11 @@ class Index:
             d_out_ids = torch.empty((nq, k), dtype=torch.int32, device=dev)
         if d_out_dist is None:
             d_out_dist = torch.empty((nq, k), dtype=torch.float32, device=dev)
-        s = C.c_void_p(stream.cuda_stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream)
+        handle = stream.cuda_stream if stream is not None else torch.cuda.current_stream(dev).cuda_stream
+        # torch's default stream has handle 0, which the C ABI reads as "the
+        # library's internal stream"; pass the legacy default stream instead so
+        # the search is ordered with the caller's work on it
+        s = C.c_void_p(handle if handle else 1)  # 1 = cudaStreamLegacy
         check(lib().dvs_search_device(self._h, device_slot, ptr(d_queries), nq, d_queries.shape[1], k, beam_width,
                                       _lib.MODE[mode], ptr(d_out_ids), ptr(d_out_dist), ptr(d_counters), s))
         return d_out_ids, d_out_dist
