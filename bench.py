@@ -54,8 +54,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--cache", default=os.environ.get("DVS_BENCH_CACHE", "/tmp/dvs_b200_bench"))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["search", "insert"], default="search",
-                    help="insert: online insert throughput into the base index (dvs_insert)")
+    ap.add_argument("--mode", choices=["search", "insert", "mixed"], default="search",
+                    help="insert: online insert throughput (dvs_insert); mixed: queries and inserts interleaved")
     ap.add_argument("--insert-count", type=int, default=100_000)
     ap.add_argument("--insert-batch", type=int, default=4096)
     ap.add_argument("--beam-width-construction", type=int, default=128)
@@ -615,12 +615,79 @@ def run_insert(args):
     print(json.dumps(line), flush=True)
 
 
+def run_mixed(args):
+    """Queries and inserts interleaved (the 50/50 query/insert serving mix): each
+    step searches --batch device-resident queries (k, beam width) and inserts
+    --insert-batch host vectors through dvs_insert (beam width construction,
+    alpha); wall clock around the pair, synchronised.  Operations/s counts both."""
+    import torch
+
+    import dvstor_b200 as D
+    from dvstor_b200 import datasets
+
+    dist = Dist("gloo")
+    wp = workload_params(args.workload, args.n)
+    L = args.beam_width or wp["search_L"]
+    k, Bq, Bi = args.k, args.batch, args.insert_batch
+    prefix = ensure_index(args, wp, 0, dist)
+    torch.cuda.set_device(0)
+    ix = D.Index(prefix, devices=(0,))
+    n0 = int(ix.info.num_vectors)
+    nsteps = args.warmup + args.steps
+    Q = torch.from_numpy(datasets.queries_for(args.workload, Bq * nsteps, stream=3)).cuda().view(nsteps, Bq, -1)
+    Xn = datasets.queries_for(args.workload, Bi * nsteps, stream=9)
+    ids = np.arange(n0, n0 + Bi * nsteps, dtype=np.uint32)
+    ix.reserve(n0 + Bi * nsteps)
+    out_i = torch.empty((Bq, k), dtype=torch.int32, device="cuda")
+    out_d = torch.empty((Bq, k), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+
+    def step(s):
+        ix.search_device(Q[s], k, L, d_out_ids=out_i, d_out_dist=out_d, stream=stream)
+        stream.synchronize()
+        ix.insert(Xn[s * Bi:(s + 1) * Bi], ids[s * Bi:(s + 1) * Bi], beam_width_construction=args.beam_width_construction,
+                  alpha=args.alpha, max_batch=Bi)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    sampler = clocks_sampler(0)
+    t_wall0 = time.time()
+    t = time.perf_counter()
+    for s in range(args.warmup, nsteps):
+        step(s)
+    torch.cuda.synchronize()
+    el = time.perf_counter() - t
+    clocks = clocks_summary(sampler, t_wall0, time.time())
+    probe = slice(Bi * args.warmup, Bi * args.warmup + 1000)
+    got, _ = ix.search(Xn[probe], 10, 64)
+    self_hit = float((got[:, 0] == ids[probe]).mean())
+    ix.close()
+    ops = (Bq + Bi) * args.steps
+    line = {
+        "metric": f"operations/sec, 50/50 queries (k={k}, L={L}) and inserts (L_c={args.beam_width_construction})",
+        "value": ops / el, "unit": "ops/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "n_base": n0, "dim": wp["dim"], "R": wp["R"], "rabitq_bits": 4,
+                   "queries_per_step": Bq, "inserts_per_step": Bi, "metric": "l2 (normalised vectors: the same "
+                   "ranking as ip; estimates and rerank are L2 in both reference modes)"},
+        "queries_per_s": Bq * args.steps / el, "inserts_per_s": Bi * args.steps / el,
+        "e2e": {"value": ops / el, "unit": "ops/s", "h2d_bytes_per_step": Bi * (wp["dim"] * 4 + 4),
+                "d2h_bytes_per_step": 0},
+        "self_hit_at_1": self_hit, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.mode == "insert":
         run_insert(args)
+    elif args.mode == "mixed":
+        run_mixed(args)
     elif args.placement == "shard":
         run_sharded(args)
     else:
