@@ -562,21 +562,24 @@ dvs_status dvs_search(dvs_index* ix, const float* h_queries, uint32_t nq, uint32
       if (r != DVS_OK) return r;
       DVS_CUDA(cudaMemcpyAsync(h_out_ids + q0 * k, d.out_ids, m * k * 4, cudaMemcpyDeviceToHost, d.stream));
       DVS_CUDA(cudaMemcpyAsync(h_out_dist + q0 * k, d.out_dist, m * k * 4, cudaMemcpyDeviceToHost, d.stream));
-      std::vector<uint32_t> cnt(m * 4);
+      // per-query counters come back only when the caller asked for statistics
+      std::vector<uint32_t> cnt(stats ? m * 4 : 0);
       uint32_t work[4] = {0, 0, 0, 0};
-      DVS_CUDA(cudaMemcpyAsync(cnt.data(), d.counters, m * 16, cudaMemcpyDeviceToHost, d.stream));
+      if (stats) DVS_CUDA(cudaMemcpyAsync(cnt.data(), d.counters, m * 16, cudaMemcpyDeviceToHost, d.stream));
       DVS_CUDA(cudaMemcpyAsync(work, d.work, 16, cudaMemcpyDeviceToHost, d.stream));
       DVS_CUDA(cudaStreamSynchronize(d.stream));
-      float ms = 0.f;
-      DVS_CUDA(cudaEventElapsedTime(&ms, d.ev0, d.ev1));
-      dvs_stats& ps = part[i];
-      for (size_t q = 0; q < m; ++q) {
-        ps.expansions += cnt[q * 4 + 0];
-        ps.estimates += cnt[q * 4 + 1];
-        ps.reranked += cnt[q * 4 + 2];
+      if (stats) {
+        float ms = 0.f;
+        DVS_CUDA(cudaEventElapsedTime(&ms, d.ev0, d.ev1));
+        dvs_stats& ps = part[i];
+        for (size_t q = 0; q < m; ++q) {
+          ps.expansions += cnt[q * 4 + 0];
+          ps.estimates += cnt[q * 4 + 1];
+          ps.reranked += cnt[q * 4 + 2];
+        }
+        ps.overflow_queries = work[2];
+        ps.device_ms = ms;
       }
-      ps.overflow_queries = work[2];
-      ps.device_ms = ms;
       if (work[1] & dvs::kErrNonFinite)
         return fail(DVS_ERR_ARG, "a query contains a non-finite value; its results are empty");
       if (work[1] & dvs::kErrCapacity)
