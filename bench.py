@@ -69,6 +69,25 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+_RESULT_FD = None
+
+
+def emit(line: dict) -> None:
+    """The one JSON result line, on the process's original stdout."""
+    fd = _RESULT_FD if _RESULT_FD is not None else sys.stdout.fileno()
+    os.write(fd, (json.dumps(line) + "\n").encode())
+
+
+def route_stdout_to_stderr() -> None:
+    """Libraries print to file descriptor 1 (NCCL announces its version there when
+    a communicator comes up); send all of it to stderr so stdout carries only the
+    result line."""
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
 class Dist:
     """torch.distributed plumbing when launched by torchrun."""
 
@@ -310,7 +329,7 @@ def run_reference(args):
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "recall_at_10": recall(ids, gt),
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_ours(args):
@@ -436,7 +455,7 @@ def run_ours(args):
             "recall_at_10": rec,
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     dist.barrier()
     dist.close()
 
@@ -545,7 +564,7 @@ def run_sharded(args):
         "recall_at_10": rec,
         "cpu_baseline": None,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_insert(args):
@@ -614,7 +633,7 @@ def run_insert(args):
         "insert_stats": stats, "self_hit_at_1": self_hit, "gpu_launches": 7 * stats["steps"],
         "clocks": clocks, "cpu_baseline": cpu,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_mixed(args):
@@ -679,11 +698,12 @@ def run_mixed(args):
                 "d2h_bytes_per_step": 0},
         "self_hit_at_1": self_hit, "clocks": clocks,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
     args = parse_args()
+    route_stdout_to_stderr()
     if args.impl == "reference":
         run_reference(args)
     elif args.mode == "insert":
