@@ -157,7 +157,9 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool 
     // 16-bit entries, 8 per 16-byte bucket; at least 2^(W-14) buckets for hash
     // width W (20 bits below 2^20 nodes, else 24).  The entry limit follows
     // slots_per_entry even where the bucket minimum is larger.
-    const uint32_t spe = slots_per_entry ? slots_per_entry : kDefaultSlots16;
+    const uint32_t spe = slots_per_entry ? slots_per_entry
+                         : search_wide_records(exact, d.lay.code_words) ? kDefaultSlotsWide
+                                                                        : kDefaultSlots16;
     s.vt16 = d.lay.n < (1u << 20) ? 20u : 24u;
     s.hbuckets = std::max(1u << (s.vt16 - 14), (cap * spe + 7) / 8);
     s.hcap = s.hbuckets * 4;
@@ -167,7 +169,8 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool 
     s.hcap = std::max(64u, (cap * spe + 31) / 32 * 32);
     s.hlimit = s.hcap / 10 * 9;
   }
-  const uint32_t words = search_warp_words(s.cap_pad, d.lay.vec_stride, s.hcap, d.lay.R);
+  const uint32_t words = search_warp_words(s.cap_pad, d.lay.vec_stride, s.hcap, d.lay.R,
+                                           search_query_layout(exact, d.lay.bits, d.lay.code_words));
   int best_warps = 0;
   for (uint32_t wpb : {1u, 2u, 4u, 8u}) {
     const size_t smem = size_t(wpb) * words * 4;

@@ -36,6 +36,10 @@ void dev_free(T*& p) {
 // for indexes of 2^24 nodes or more, compact 16-bit table below) and the spill table.
 constexpr uint32_t kDefaultSlots32 = 48;
 constexpr uint32_t kDefaultSlots16 = 48;
+// Records wider than 128 bytes: a smaller table buys resident warps (7 instead
+// of 5 per SM for 960-dim 4-bit records at beam capacity 264), and a spill
+// costs little next to estimating such records.
+constexpr uint32_t kDefaultSlotsWide = 40;
 constexpr uint32_t kOverflowSlots = 1u << 14;
 
 struct Device {

@@ -208,68 +208,103 @@ __device__ __forceinline__ void code_word(uint32_t word, uint32_t wi, int e, con
   }
 }
 
-// Chain t of one record's estimate, computed by lane t of a lane quad: the
-// reference kernel's own tile-of-4 split (lane t sums dims j = t mod 4 for
-// B in {1,2,4}, char4 steps c = t mod 4 for B = 8), in ascending order.  Used
-// for records wider than 128 bytes, where one lane per record would leave
-// lanes idle and unroll too much code.  Lane 0 also returns the record's add
-// and rescale factors.
+// Chain t of two records' estimates (ids cA and cB; cB may repeat cA when the
+// round has no second record), computed by lane t of a lane quad: the
+// reference kernel's own tile-of-4 split (lane t sums dims j = t mod 4 for B in
+// {1,2,4}, char4 steps c = t mod 4 for B = 8), each chain in ascending order.
+// Used for records wider than 128 bytes.  The two chains are independent, so
+// their loads and FMAs interleave; each q' read serves both.  For B in {1,2,4}
+// `q` is this lane's chain of the chain-major q' (position p = dim 4p + t), for
+// B = 8 the dimension-order q'.  Lane 0 also returns the records' add and
+// rescale factors.
 template <int BITS>
-__device__ __forceinline__ float estimate_quad_chain(const DevLayout& ix, uint32_t c, const float* __restrict__ qr,
-                                                     uint32_t t, float& add_o, float& rs_o) {
-  const uint32_t* r = reinterpret_cast<const uint32_t*>(rec_row(ix, c));
+__device__ __forceinline__ void estimate_quad_chain2(const DevLayout& ix, uint32_t cA, uint32_t cB,
+                                                     const float* __restrict__ q, uint32_t t, float& sA, float& sB,
+                                                     float (&fA)[2], float (&fB)[2]) {
+  const uint32_t* rA = reinterpret_cast<const uint32_t*>(rec_row(ix, cA));
+  const uint32_t* rB = reinterpret_cast<const uint32_t*>(rec_row(ix, cB));
   if (t == 0) {
-    add_o = __uint_as_float(__ldg(r + ix.code_words));
-    rs_o = __uint_as_float(__ldg(r + ix.code_words + 1));
+    fA[0] = __uint_as_float(__ldg(rA + ix.code_words));
+    fA[1] = __uint_as_float(__ldg(rA + ix.code_words + 1));
+    fB[0] = __uint_as_float(__ldg(rB + ix.code_words));
+    fB[1] = __uint_as_float(__ldg(rB + ix.code_words + 1));
   }
-  float s = 0.f;
+  sA = 0.f;
+  sB = 0.f;
   if constexpr (BITS == 8) {
-    // lane t takes words t, t+4, ...: 16 of them in flight per batch
+    // lane t takes words t, t+4, ...: 8 of each record in flight per batch
     const uint32_t nw = ix.dim >> 2;
-    for (uint32_t w0 = t; w0 < nw; w0 += 64) {
-      uint32_t a[16];
+    for (uint32_t w0 = t; w0 < nw; w0 += 32) {
+      uint32_t a[8], b[8];
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (w0 + 4 * k < nw) a[k] = __ldg(r + w0 + 4 * k);
+      for (int k = 0; k < 8; ++k)
+        if (w0 + 4 * k < nw) {
+          a[k] = __ldg(rA + w0 + 4 * k);
+          b[k] = __ldg(rB + w0 + 4 * k);
+        }
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (w0 + 4 * k < nw)
-          s = __fadd_rn(s, rabitq_char4(a[k], *reinterpret_cast<const float4*>(qr + 4 * (w0 + 4 * k))));
+      for (int k = 0; k < 8; ++k)
+        if (w0 + 4 * k < nw) {
+          const float4 q4 = *reinterpret_cast<const float4*>(q + 4 * (w0 + 4 * k));
+          sA = __fadd_rn(sA, rabitq_char4(a[k], q4));
+          sB = __fadd_rn(sB, rabitq_char4(b[k], q4));
+        }
     }
   } else {
+    // a 16-byte chunk holds kPer = 32/B dims of each of the 4 chains: positions
+    // kPer*ch .. kPer*ch + kPer-1 of this lane's chain, word e giving kPer/4 of them
     constexpr uint32_t kPer = 32 / BITS, kMask = (1u << BITS) - 1u;
-    const uint4* r4 = reinterpret_cast<const uint4*>(r);
-    const uint32_t nch = (ix.dim / kPer) >> 2;  // 16-byte chunks whose every dim is < dim
+    const uint4* a4 = reinterpret_cast<const uint4*>(rA);
+    const uint4* b4 = reinterpret_cast<const uint4*>(rB);
+    const uint32_t nch = (ix.dim / kPer) >> 2;  // chunks whose every dim is < dim
     const uint32_t sh0 = BITS * t;
-    // 16 chunks (256 bytes of codes) in flight per batch
-    for (uint32_t ch = 0; ch < nch; ch += 16) {
-      uint4 v[16];
+    for (uint32_t ch = 0; ch < nch; ch += 8) {
+      uint4 va[8], vb[8];
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
-        if (ch + k < nch) v[k] = __ldg(r4 + ch + k);
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
+      for (int k = 0; k < 8; ++k)
         if (ch + k < nch) {
-          const uint32_t wv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+          va[k] = __ldg(a4 + ch + k);
+          vb[k] = __ldg(b4 + ch + k);
+        }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (ch + k < nch) {
+          float qf[kPer];
+          const float4* q4 = reinterpret_cast<const float4*>(q + (ch + k) * kPer);
+#pragma unroll
+          for (uint32_t g = 0; g < kPer / 4; ++g) {
+            const float4 f = q4[g];
+            qf[4 * g] = f.x;
+            qf[4 * g + 1] = f.y;
+            qf[4 * g + 2] = f.z;
+            qf[4 * g + 3] = f.w;
+          }
+          const uint32_t wa[4] = {va[k].x, va[k].y, va[k].z, va[k].w};
+          const uint32_t wb[4] = {vb[k].x, vb[k].y, vb[k].z, vb[k].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float* q = qr + ((ch + k) * 4 + e) * kPer + t;
 #pragma unroll
-            for (uint32_t i = 0; i < kPer / 4; ++i)
-              s = __fmaf_rn(small_u2f((wv[e] >> (sh0 + 4 * BITS * i)) & kMask), q[4 * i], s);
+            for (uint32_t i = 0; i < kPer / 4; ++i) {
+              const uint32_t sh = sh0 + 4 * BITS * i;
+              const float qv = qf[e * (kPer / 4) + i];
+              sA = __fmaf_rn(small_u2f((wa[e] >> sh) & kMask), qv, sA);
+              sB = __fmaf_rn(small_u2f((wb[e] >> sh) & kMask), qv, sB);
+            }
           }
         }
       }
     }
     // words past the last whole chunk, the partial last word included
     for (uint32_t wi = nch * 4; wi * kPer < ix.dim; ++wi) {
-      const uint32_t word = __ldg(r + wi);
+      const uint32_t wa = __ldg(rA + wi), wb = __ldg(rB + wi);
       const uint32_t j0 = wi * kPer;
-      for (uint32_t n = t; n < kPer && j0 + n < ix.dim; n += 4)
-        s = __fmaf_rn(small_u2f((word >> (BITS * n)) & kMask), qr[j0 + n], s);
+      for (uint32_t n = t; n < kPer && j0 + n < ix.dim; n += 4) {
+        const float qv = q[(j0 + n) >> 2];
+        sA = __fmaf_rn(small_u2f((wa >> (BITS * n)) & kMask), qv, sA);
+        sB = __fmaf_rn(small_u2f((wb >> (BITS * n)) & kMask), qv, sB);
+      }
     }
   }
-  return s;
 }
 
 // Exact L2 of `count` rows (slot ids in `rows`) against q, written to `out`;
@@ -343,14 +378,17 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
   extern __shared__ __align__(16) uint32_t smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const DevLayout& ix = a.ix;
-  uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R);
+  constexpr uint32_t qlayout = EXACT ? kQueryRaw : (RCH == 0 && BITS != 8 ? kQueryChain : kQueryRot);
+  uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R, qlayout);
   float* bdA = reinterpret_cast<float*>(base);
   uint32_t* biA = base + a.cap_pad;
   float* bdB = reinterpret_cast<float*>(base + 2 * a.cap_pad);
   uint32_t* biB = base + 3 * a.cap_pad;
+  // exact_gpu: the query (qv); rabitq_gpu: q' (qr) in dimension or chain order
   float* qv = reinterpret_cast<float*>(base + 4 * a.cap_pad);
-  float* qr = qv + a.dim_pad;
-  uint32_t* cid = base + 4 * a.cap_pad + 2 * a.dim_pad;
+  float* qr = qv;
+  const uint32_t cs = chain_stride(a.dim_pad);
+  uint32_t* cid = base + 4 * a.cap_pad + (qlayout == kQueryChain ? 4 * cs : a.dim_pad);
   float* cd = reinterpret_cast<float*>(cid + 32 * NPL);
   float* sd = reinterpret_cast<float*>(cid + 64 * NPL);
   uint32_t* sid = cid + 96 * NPL;
@@ -370,11 +408,16 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
 
     // ---- per-query set-up ----
     bool finite = true;
+    const float* qg = a.queries + size_t(qi) * dim;
     for (uint32_t j = lane; j < a.dim_pad; j += 32) {
-      const float x = j < dim ? a.queries[size_t(qi) * dim + j] : 0.f;
+      const float x = j < dim ? qg[j] : 0.f;
       finite &= isfinite(x);
-      qv[j] = x;
-      qr[j] = rabitq ? a.qrot[size_t(qi) * ix.vec_stride + j] : 0.f;
+      if constexpr (qlayout == kQueryRaw) {
+        qv[j] = x;
+      } else {
+        const float y = a.qrot[size_t(qi) * ix.vec_stride + j];
+        qr[qlayout == kQueryChain ? (j & 3) * cs + (j >> 2) : j] = y;
+      }
     }
     const bool nonfinite = !__all_sync(kFull, finite);
     float q_add = 0.f, q_k1 = 0.f;
@@ -388,7 +431,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       for (uint32_t j = lane; j < (a.hcap >> 2); j += 32) h4[j] = e;
     }
     __syncwarp();
-    const float md = seed_distance_warp(qv, vec_row(ix, ix.medoid), dim, ix.metric == 1, lane);
+    const float md = seed_distance_warp(rabitq ? qg : qv, vec_row(ix, ix.medoid), dim, ix.metric == 1, lane);
     if (lane == 0) {
       bdA[0] = md;
       biA[0] = ix.medoid;
@@ -540,14 +583,23 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       if (!rabitq) {
         l2_rows_warp(ix, qv, cid, m, cd, lane, 0xFFFFFFFFu);
       } else if (RCH == 0) {
-        // wide records: 8 per round, a lane quad each, chains reduced with the tile butterfly
+        // wide records: 16 per round, two per lane quad (candidates i and
+        // i + 8), chains reduced with the tile butterfly
         const uint32_t t = lane & 3;
-        for (uint32_t i0 = 0; i0 < m; i0 += 8) {
-          const uint32_t i = i0 + (lane >> 2);
-          float part = 0.f, add_o = 0.f, rs_o = 0.f;
-          if (i < m) part = estimate_quad_chain<BITS>(ix, cid[i], qr, t, add_o, rs_o);
-          const float dot = quad_butterfly(part);
-          if (i < m && t == 0) cd[i] = rabitq_finish(dot, add_o, rs_o, q_add, q_k1, float((1u << BITS) - 1u));
+        const float* qt = qlayout == kQueryChain ? qr + t * cs : qr;
+        for (uint32_t i0 = 0; i0 < m; i0 += 16) {
+          const uint32_t iA = i0 + (lane >> 2), iB = iA + 8;
+          float pA = 0.f, pB = 0.f, fA[2] = {0.f, 0.f}, fB[2] = {0.f, 0.f};
+          if (iA < m) {
+            const uint32_t cA = cid[iA];
+            estimate_quad_chain2<BITS>(ix, cA, iB < m ? cid[iB] : cA, qt, t, pA, pB, fA, fB);
+          }
+          const float dA = quad_butterfly(pA), dB = quad_butterfly(pB);
+          if (t == 0) {
+            const float top = float((1u << BITS) - 1u);
+            if (iA < m) cd[iA] = rabitq_finish(dA, fA[0], fA[1], q_add, q_k1, top);
+            if (iB < m) cd[iB] = rabitq_finish(dB, fB[0], fB[1], q_add, q_k1, top);
+          }
         }
       }
       __syncwarp();
@@ -651,8 +703,12 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
     // ---- rerank (vamana.hh:358-422) and final order (vamana.hh:424-446) ----
     uint32_t Cr = 0;
     if (rabitq && nb > 0) {
+      // the query goes into the visited table's words, dead once the search ends
+      float* qx = reinterpret_cast<float*>(htab);
       __syncwarp();
-      l2_rows_warp(ix, qv, bi, nb, bd, lane, ~kExpandedBit);
+      for (uint32_t j = lane; j < a.dim_pad; j += 32) qx[j] = j < dim ? qg[j] : 0.f;
+      __syncwarp();
+      l2_rows_warp(ix, qx, bi, nb, bd, lane, ~kExpandedBit);
       Cr = nb;
       __syncwarp();
       for (uint32_t p = lane; p < nb; p += 32) {
@@ -795,6 +851,13 @@ void launch_rch(int rch, const SearchArgs& a, dim3 g, dim3 b, size_t smem, cudaS
 
 }  // namespace
 
+uint32_t search_query_layout(bool exact, uint32_t bits, uint32_t code_words) {
+  if (exact) return kQueryRaw;
+  return record_chunks(code_words) == 0 && bits != 8 ? kQueryChain : kQueryRot;
+}
+
+bool search_wide_records(bool exact, uint32_t code_words) { return !exact && record_chunks(code_words) == 0; }
+
 cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, bool exact, uint32_t wpb, size_t smem,
                              int* bps) {
   const bool two = R > 32;
@@ -810,7 +873,10 @@ cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, boo
 }
 
 cudaError_t launch_search(const SearchArgs& a, uint32_t wpb, uint32_t blocks, cudaStream_t stream) {
-  const size_t smem = size_t(wpb) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, a.ix.R) * 4;
+  const size_t smem = size_t(wpb) *
+                     search_warp_words(a.cap_pad, a.dim_pad, a.hcap, a.ix.R,
+                                       search_query_layout(a.mode == 1, a.ix.bits, a.ix.code_words)) *
+                     4;
   const bool two = a.ix.R > 32;
   const int rch = record_chunks(a.ix.code_words);
   const dim3 grid(blocks), block(wpb * 32);

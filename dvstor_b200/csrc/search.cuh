@@ -89,12 +89,34 @@ constexpr uint32_t kErrHopLimit = 2u;
 constexpr uint32_t kErrTimeout = 4u;
 constexpr uint32_t kErrNonFinite = 8u;  // the query held a NaN or an infinity: no search, empty results
 
+// How a search warp holds its query in shared memory.
+//   kQueryRaw:   exact_gpu; the query itself, read by every distance.
+//   kQueryRot:   rabitq_gpu; the rotated query q' in dimension order.
+//   kQueryChain: rabitq_gpu with wide 1/2/4-bit records; q' chain-major: chain
+//                t (dims j = t mod 4, the dims one lane of a record's lane quad
+//                sums) is contiguous, so a lane reads its chain 16 bytes at a
+//                time.
+// In both rabitq layouts the query itself is not resident during the search:
+// the seed distance reads it from global memory and the rerank copies it into
+// the visited table's words, which are dead by then.
+constexpr uint32_t kQueryRaw = 0, kQueryRot = 1, kQueryChain = 2;
+
+// Words between the starts of two chains of a chain-major q': at least
+// dim_pad / 4, and 4 mod 8 so that the four chains' 16-byte reads at one
+// position fall in four distinct bank groups.
+__host__ __device__ inline uint32_t chain_stride(uint32_t dim_pad) { return ((dim_pad / 4 + 3) & ~7u) + 4; }
+
 // Words of shared memory one warp of the search kernel uses: two beams (cap_pad
-// distances + ids each), query and rotated query, four candidate staging arrays
-// of 32 x slots-per-lane entries (slots per lane = 2 when R > 32, else 1), the
-// visited table.
-__host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R) {
-  return 4 * cap_pad + 2 * dim_pad + (R > 32 ? 256 : 128) + hcap;
+// distances + ids each), the query in the given layout, four candidate staging
+// arrays of 32 x slots-per-lane entries (slots per lane = 2 when R > 32, else
+// 1), the visited table (at least dim_pad words in the rabitq layouts, which
+// put the query there for the rerank).  Every part is a multiple of 4 words, so
+// each starts 16-byte aligned.
+__host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R,
+                                                      uint32_t qlayout) {
+  const uint32_t qwords = qlayout == kQueryChain ? 4 * chain_stride(dim_pad) : dim_pad;
+  const uint32_t twords = qlayout == kQueryRaw ? hcap : (hcap > dim_pad ? hcap : dim_pad);
+  return 4 * cap_pad + qwords + (R > 32 ? 256 : 128) + twords;
 }
 
 // q' = P^T q (the sequential fmaf chain over i per output) and the query
@@ -121,6 +143,14 @@ cudaError_t launch_search(const SearchArgs& a, uint32_t warps_per_block, uint32_
 // per-warp shared memory; also sets the kernel's dynamic smem attribute.
 cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, bool exact, uint32_t warps_per_block,
                              size_t smem_bytes, int* blocks_per_sm);
+
+// The query layout (kQueryRaw / kQueryRot / kQueryChain) of the search kernel
+// instantiation that serves this mode and record shape.
+uint32_t search_query_layout(bool exact, uint32_t bits, uint32_t code_words);
+
+// Whether that instantiation loads records after the visited check (records
+// wider than 128 bytes) rather than holding them in registers.
+bool search_wide_records(bool exact, uint32_t code_words);
 
 }  // namespace dvs
 
