@@ -246,8 +246,12 @@ def bytes_per_query(dim, R, bits, k, H, E, Cr, nq):
     return 4 * dim + H * (4 * R + 1) + E * s_code + Cr * 4 * dim + 4 * dim * dim / nq + 8 * k
 
 
-def profile_traffic():
-    """DRAM bytes per launch of the search kernel from the committed ncu summary."""
+def profile_traffic(args, wp):
+    """DRAM bytes per launch of the search kernel from the committed ncu summary,
+    which covers the default workload only (None for any other configuration)."""
+    if (args.workload, wp["n"], args.batch, args.k, args.beam_width) != (
+            WORKLOAD, workload_params(WORKLOAD)["n"], BATCH, 10, None):
+        return None
     try:
         for ln in open(PROFILE_SUMMARY):
             if ln.startswith("traffic_bytes_per_launch_full_workload="):
@@ -390,7 +394,7 @@ def run_ours(args):
     search_avg_ms = search_ms / max(n_search, 1)
     achieved = bq * B / (search_avg_ms / 1e3) / 1e9
     peak, peak_kind = hbm_peak()
-    tr = profile_traffic()
+    tr = profile_traffic(args, wp)
 
     # ---- end to end through the host API ----
     # every step's queries are staged in pinned host memory before timing; a

@@ -80,6 +80,62 @@ __device__ __forceinline__ float l2_quad_partial(const float* __restrict__ q, co
   return acc;
 }
 
+// l2_quad_partial of two rows at once (xB may equal xA): the same chain per
+// row, the two chains interleaved so their loads and FMAs overlap, each q
+// chunk read once for both.
+__device__ __forceinline__ void l2_quad_partial2(const float* __restrict__ q, const float* __restrict__ xA,
+                                                 const float* __restrict__ xB, uint32_t dim, uint32_t t, float& accA,
+                                                 float& accB) {
+  const uint32_t n4 = dim >> 2;
+  const float4* q4 = reinterpret_cast<const float4*>(q);
+  const float4* a4 = reinterpret_cast<const float4*>(xA);
+  const float4* b4 = reinterpret_cast<const float4*>(xB);
+  float sa = 0.f, sb = 0.f;
+#define DVS_ACC4_2(Q, A, B)                                              \
+  {                                                                      \
+    float d;                                                             \
+    d = __fsub_rn(Q.x, A.x); sa = __fmaf_rn(d, d, sa);                   \
+    d = __fsub_rn(Q.x, B.x); sb = __fmaf_rn(d, d, sb);                   \
+    d = __fsub_rn(Q.y, A.y); sa = __fmaf_rn(d, d, sa);                   \
+    d = __fsub_rn(Q.y, B.y); sb = __fmaf_rn(d, d, sb);                   \
+    d = __fsub_rn(Q.z, A.z); sa = __fmaf_rn(d, d, sa);                   \
+    d = __fsub_rn(Q.z, B.z); sb = __fmaf_rn(d, d, sb);                   \
+    d = __fsub_rn(Q.w, A.w); sa = __fmaf_rn(d, d, sa);                   \
+    d = __fsub_rn(Q.w, B.w); sb = __fmaf_rn(d, d, sb);                   \
+  }
+  uint32_t i = t;
+  // four chunks of each row per trip in flight
+  for (; i + 12 < n4; i += 16) {
+    float4 a[4], b[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      a[k] = __ldg(a4 + i + 4 * k);
+      b[k] = __ldg(b4 + i + 4 * k);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 c = q4[i + 4 * k];
+      DVS_ACC4_2(c, a[k], b[k])
+    }
+  }
+  for (; i < n4; i += 4) {
+    const float4 a = __ldg(a4 + i), b = __ldg(b4 + i);
+    const float4 c = q4[i];
+    DVS_ACC4_2(c, a, b)
+  }
+#undef DVS_ACC4_2
+  const uint32_t tail = (n4 << 2) + t;
+  if (tail < dim) {
+    const float qt = q[tail];
+    float d = __fsub_rn(qt, __ldg(xA + tail));
+    sa = __fmaf_rn(d, d, sa);
+    d = __fsub_rn(qt, __ldg(xB + tail));
+    sb = __fmaf_rn(d, d, sb);
+  }
+  accA = sa;
+  accB = sb;
+}
+
 // Same chain order on a single thread (all four lanes' chains), for callers that
 // give one thread a whole row.
 __device__ __forceinline__ float l2_single(const float* __restrict__ q, const float* __restrict__ x, uint32_t dim) {

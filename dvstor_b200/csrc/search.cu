@@ -308,20 +308,25 @@ __device__ __forceinline__ void estimate_quad_chain2(const DevLayout& ix, uint32
 }
 
 // Exact L2 of `count` rows (slot ids in `rows`) against q, written to `out`;
-// 4 lanes per row, 8 rows per round.  Warp-uniform control flow.
+// 4 lanes per row, two rows per lane quad (rows i and i + 8), 16 rows per
+// round.  Warp-uniform control flow.
 __device__ __forceinline__ void l2_rows_warp(const DevLayout& ix, const float* __restrict__ q,
                                              const uint32_t* rows, uint32_t count, float* out, uint32_t lane,
                                              uint32_t row_mask) {
   const uint32_t t = lane & 3;
-  for (uint32_t r0 = 0; r0 < count; r0 += 8) {
-    const uint32_t i = r0 + (lane >> 2);
-    float part = 0.f;
-    if (i < count) {
-      const uint32_t row = rows[i] & row_mask;
-      part = l2_quad_partial(q, vec_row(ix, row), ix.dim, t);
+  for (uint32_t r0 = 0; r0 < count; r0 += 16) {
+    const uint32_t iA = r0 + (lane >> 2), iB = iA + 8;
+    float pA = 0.f, pB = 0.f;
+    if (iA < count) {
+      const float* xA = vec_row(ix, rows[iA] & row_mask);
+      const float* xB = iB < count ? vec_row(ix, rows[iB] & row_mask) : xA;
+      l2_quad_partial2(q, xA, xB, ix.dim, t, pA, pB);
     }
-    const float total = quad_butterfly(part);
-    if (i < count && t == 0) out[i] = total;
+    const float tA = quad_butterfly(pA), tB = quad_butterfly(pB);
+    if (t == 0) {
+      if (iA < count) out[iA] = tA;
+      if (iB < count) out[iB] = tB;
+    }
   }
 }
 
@@ -362,11 +367,13 @@ __device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n,
 
 // Register cap of a search_kernel instantiation.  R <= 32 with records held in
 // registers: 128, four warps per SM sub-partition (16,384 registers each), so
-// that shared memory (13 warps with the compact visited table at L = 64), not
-// registers, bounds the warps per SM; the others are bounded by shared memory
-// or need their registers, and keep up to 255.
+// that shared memory (14 warps with the compact visited table at L = 64), not
+// registers, bounds the warps per SM.  Records loaded after the visited check
+// (wider than 128 bytes): 168, three warps per sub-partition (12 per SM, what
+// shared memory allows for 768-dim records at L = 64).  The rest are bounded
+// by shared memory or need their registers, and keep up to 255.
 __host__ __device__ constexpr int search_max_regs(int npl, int rch, bool exact) {
-  return npl == 1 && (rch > 0 || exact) ? 128 : 255;
+  return npl == 1 && (rch > 0 || exact) ? 128 : (rch == 0 && !exact) ? 168 : 255;
 }
 
 // EXACT: exact_gpu (exact distances, no records; BITS and RCH unused) or
