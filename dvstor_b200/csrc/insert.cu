@@ -29,6 +29,7 @@
 #include <vector>
 
 #include <cub/cub.cuh>
+#include <cuda_pipeline.h>
 
 #include "device_math.cuh"
 #include "index_state.h"
@@ -73,38 +74,15 @@ __device__ __forceinline__ float chain_l2(const float* __restrict__ a, const flo
   return d;
 }
 
-// Lane t's share of batch_l2_squared_distance_kernel<4> (the order of
-// l2_quad_partial: float4 chunks t, t+4, ... then tail dim n4*4 + t, diff = q - x)
-// with plain loads, so x may be in shared memory.
-__device__ __forceinline__ float l2_quad_any(const float* q, const float* x, uint32_t dim, uint32_t t) {
-  const uint32_t n4 = dim >> 2;
-  const float4* q4 = reinterpret_cast<const float4*>(q);
-  const float4* x4 = reinterpret_cast<const float4*>(x);
-  float acc = 0.f;
-  for (uint32_t i = t; i < n4; i += 4) {
-    const float4 a = x4[i], b = q4[i];
-    float d = __fsub_rn(b.x, a.x);
-    acc = __fmaf_rn(d, d, acc);
-    d = __fsub_rn(b.y, a.y);
-    acc = __fmaf_rn(d, d, acc);
-    d = __fsub_rn(b.z, a.z);
-    acc = __fmaf_rn(d, d, acc);
-    d = __fsub_rn(b.w, a.w);
-    acc = __fmaf_rn(d, d, acc);
-  }
-  const uint32_t tail = (n4 << 2) + t;
-  if (tail < dim) {
-    const float d = __fsub_rn(q[tail], x[tail]);
-    acc = __fmaf_rn(d, d, acc);
-  }
-  return acc;
-}
-
 constexpr uint32_t kQuantPerBlock = 8;    // vectors per quantize block (one lane quad each)
 constexpr uint32_t kPruneThreads = 128;
 constexpr uint32_t kRevWarps = 4;         // warps (targets in flight) per reverse-edge block
 constexpr uint32_t kMaxAll = 65;          // R + 1 candidates of an overflow prune (R <= 64)
 constexpr size_t kStageBudget = 160 * 1024;  // shared memory for staged candidate vectors per block
+// largest reverse-edge warp that stages its candidate rows (768-dim rows at
+// R = 32 still do: two warps per SM reading shared memory beat many warps
+// reading each candidate row from L2 at every greedy step)
+constexpr size_t kRevStageMax = 120 * 1024;
 
 // rabitq_quantize_single_kernel<4,B> (src/gpu/kernels/distance_kernels.cuh:376-464)
 // on rotated rows: lane t of a quad takes dims j = t mod 4; tile sums by the
@@ -186,13 +164,19 @@ __global__ void __launch_bounds__(32) insert_quantize_kernel(const float* __rest
   }
 }
 
+// float4s between the starts of two staged candidate rows of a prune:
+// vec_stride / 4 rounded up to odd, so threads reading consecutive rows at one
+// offset fall in distinct banks.
+__host__ __device__ inline uint32_t prune_row_stride4(uint32_t vec_stride) { return (vec_stride >> 2) | 1u; }
+
 // robust_prune_kernel (src/gpu/kernels/distance_kernels.cuh:285-370) for new
 // vector v: its final beam (slots by ascending distance, from the search) is
 // the candidate list; the nearest valid candidate is kept and every later
 // valid p' with alpha * |p* - p'|^2 <= d(v, p') is dropped, until R are kept.
 // The kept slots are the new node's adjacency row (row0 + v).  STAGED: the
-// candidates' vectors are copied to shared memory once (when Lc rows fit), so
-// the greedy loop reads no global memory.
+// candidates' vectors are copied to shared memory once (cp.async, when Lc rows
+// fit) at an odd float4 stride, so the greedy loop reads no global memory and
+// threads reading consecutive candidates hit distinct banks.
 template <bool STAGED>
 __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLayout ix, const uint32_t* __restrict__ cand,
                                                                      const float* __restrict__ cand_d,
@@ -201,8 +185,9 @@ __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLa
                                                                      uint32_t* __restrict__ adj) {
   extern __shared__ __align__(16) float sm[];
   const uint32_t v = blockIdx.x, tid = threadIdx.x, R = ix.R, dim = ix.dim, vs = ix.vec_stride;
-  float* rows = sm;                                    // STAGED: Lc candidate vectors; else p*'s vector
-  float* dd = rows + (STAGED ? size_t(Lc) * vs : vs);  // candidate distances
+  const uint32_t rs = 4 * prune_row_stride4(vs);             // floats between staged rows
+  float* rows = sm;                                          // STAGED: Lc candidate vectors; else p*'s vector
+  float* dd = rows + (STAGED ? size_t(Lc) * rs : vs);        // candidate distances
   uint32_t* sl = reinterpret_cast<uint32_t*>(dd + Lc);  // candidate slots
   uint8_t* valid = reinterpret_cast<uint8_t*>(sl + Lc);
   const uint32_t n = counters[size_t(v) * 4 + 3] & 0xFFFFu;
@@ -218,12 +203,14 @@ __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLa
     return;
   }
   if (STAGED) {
-    const uint32_t c4 = vs >> 2, lane = tid & 31;
-    for (uint32_t r = tid >> 5; r < n; r += blockDim.x >> 5) {
-      const float4* src = reinterpret_cast<const float4*>(vec_row(ix, sl[r]));
-      float4* dst = reinterpret_cast<float4*>(rows + size_t(r) * vs);
-      for (uint32_t c = lane; c < c4; c += 32) dst[c] = src[c];
+    const uint32_t c4 = vs >> 2;
+    for (uint32_t idx = tid; idx < n * c4; idx += blockDim.x) {
+      const uint32_t r = idx / c4, c = idx - r * c4;
+      __pipeline_memcpy_async(reinterpret_cast<float4*>(rows + size_t(r) * rs) + c,
+                              reinterpret_cast<const float4*>(vec_row(ix, sl[r])) + c, 16);
     }
+    __pipeline_commit();
+    __pipeline_wait_prior(0);
     __syncthreads();
   }
   uint32_t kept = 0;  // identical in every thread
@@ -232,7 +219,7 @@ __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLa
     const uint32_t pslot = sl[s];
     if (tid == 0) row[kept] = pslot;
     ++kept;
-    const float* pv = rows + size_t(s) * vs;
+    const float* pv = rows + size_t(s) * rs;
     if (!STAGED) {
       const float* g = vec_row(ix, pslot);
       for (uint32_t k = tid; k < dim; k += blockDim.x) rows[k] = g[k];
@@ -241,7 +228,7 @@ __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLa
     }
     for (uint32_t i = s + 1 + tid; i < n; i += blockDim.x) {
       if (!valid[i]) continue;
-      const float d = chain_l2(pv, STAGED ? rows + size_t(i) * vs : vec_row(ix, sl[i]), dim);
+      const float d = chain_l2(pv, STAGED ? rows + size_t(i) * rs : vec_row(ix, sl[i]), dim);
       if (__fmul_rn(alpha, d) <= dd[i]) valid[i] = 0;
     }
     __syncthreads();
@@ -257,6 +244,13 @@ struct RevWarp {
   uint32_t kept[64];
   uint8_t valid[kMaxAll + 3];
 };
+constexpr size_t kRevWarpBytes = (sizeof(RevWarp) + 15) / 16 * 16;
+
+// Shared memory of one reverse-edge warp: its RevWarp, then (STAGED) the R + 1
+// candidate rows.
+__host__ __device__ inline size_t rev_warp_bytes(uint32_t R, uint32_t vec_stride, bool staged) {
+  return kRevWarpBytes + (staged ? size_t(R + 1) * prune_row_stride4(vec_stride) * 16 : 0);
+}
 
 // Reverse edges (vamana.hh:795-986): warp w takes old node targets[w] and
 // applies the new slots srcs[offs[w] .. offs[w+1]) in insert order (*nruns
@@ -264,6 +258,10 @@ struct RevWarp {
 // the new slot appended; a full one is replaced by RobustPrune of its R
 // neighbours plus the new node, from the target's vector, with the distances
 // of batch_l2_squared_distance_kernel<4> ordered by (distance, position).
+// The candidates' vectors are read from global memory for those distances
+// (two per lane quad); STAGED then copies them to shared memory in rank order
+// (cp.async), so that in the greedy loop lane l reads rank s + 1 + l, rows at
+// an odd float4 stride: no bank conflicts, the pivot row a broadcast.
 // stats[2] counts the overflow prunes, stats[3] keeps the largest group.
 template <bool STAGED>
 __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const DevLayout ix, uint32_t* __restrict__ adj,
@@ -272,12 +270,12 @@ __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const Dev
                                                                        const uint32_t* __restrict__ srcs,
                                                                        const uint32_t* __restrict__ nruns, float alpha,
                                                                        unsigned long long* __restrict__ stats) {
-  __shared__ RevWarp ws[kRevWarps];
-  extern __shared__ __align__(16) float rows_all[];  // STAGED: R + 1 vectors per warp
+  extern __shared__ __align__(16) uint8_t rev_smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  RevWarp& W = ws[wib];
-  const uint32_t R = ix.R, dim = ix.dim, vs = ix.vec_stride;
-  float* rows = rows_all + size_t(wib) * (R + 1) * vs;
+  const uint32_t R = ix.R, dim = ix.dim, c4 = ix.vec_stride >> 2, s4 = prune_row_stride4(ix.vec_stride);
+  uint8_t* mine = rev_smem + size_t(wib) * rev_warp_bytes(R, ix.vec_stride, STAGED);
+  RevWarp& W = *reinterpret_cast<RevWarp*>(mine);
+  float4* rows = reinterpret_cast<float4*>(mine + kRevWarpBytes);
   const uint32_t wpb = blockDim.x >> 5;
   const uint32_t ntargets = *nruns;
   for (uint32_t w = blockIdx.x * wpb + wib; w < ntargets; w += gridDim.x * wpb) {
@@ -285,6 +283,7 @@ __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const Dev
     if (tg == kEmptySlot) continue;
     uint32_t* row = adj + size_t(tg) * R;
     if (lane == 0) atomicMax(stats + 3, static_cast<unsigned long long>(offs[w + 1] - offs[w]));
+    const float* tv = vec_row(ix, tg);
     for (uint32_t e = offs[w]; e < offs[w + 1]; ++e) {
       const uint32_t v = srcs[e];
       const uint32_t a0 = lane < R ? row[lane] : kEmptySlot;
@@ -303,26 +302,19 @@ __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const Dev
       if (lane + 32 < R) W.all[lane + 32] = a1;
       if (lane == 0) W.all[R] = v;
       __syncwarp();
-      if (STAGED) {
-        const uint32_t c4 = vs >> 2;
-        for (uint32_t r = 0; r < n_all; ++r) {
-          const float4* src = reinterpret_cast<const float4*>(vec_row(ix, W.all[r]));
-          float4* dst = reinterpret_cast<float4*>(rows + size_t(r) * vs);
-          for (uint32_t c = lane; c < c4; c += 32) dst[c] = src[c];
+      for (uint32_t i0 = 0; i0 < n_all; i0 += 16) {
+        const uint32_t iA = i0 + (lane >> 2), iB = iA + 8;
+        float pA = 0.f, pB = 0.f;
+        if (iA < n_all) {
+          const float* xA = vec_row(ix, W.all[iA]);
+          const float* xB = iB < n_all ? vec_row(ix, W.all[iB]) : xA;
+          l2_quad_partial2(tv, xA, xB, dim, lane & 3, pA, pB);
         }
-        __syncwarp();
-      }
-      auto cand_row = [&](uint32_t i) -> const float* {
-        return STAGED ? rows + size_t(i) * vs : vec_row(ix, W.all[i]);
-      };
-      const float* tv = vec_row(ix, tg);
-      for (uint32_t i0 = 0; i0 < n_all; i0 += 8) {
-        const uint32_t i = i0 + (lane >> 2);
-        const float part = i < n_all ? (STAGED ? l2_quad_any(tv, cand_row(i), dim, lane & 3)
-                                               : l2_quad_partial(tv, cand_row(i), dim, lane & 3))
-                                     : 0.f;
-        const float tot = quad_butterfly(part);
-        if (i < n_all && (lane & 3) == 0) W.d[i] = tot;
+        const float tA = quad_butterfly(pA), tB = quad_butterfly(pB);
+        if ((lane & 3) == 0) {
+          if (iA < n_all) W.d[iA] = tA;
+          if (iB < n_all) W.d[iB] = tB;
+        }
       }
       __syncwarp();
       for (uint32_t i = lane; i < n_all; i += 32) {
@@ -334,16 +326,28 @@ __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const Dev
         W.valid[rk] = 1;
       }
       __syncwarp();
+      if (STAGED) {
+        for (uint32_t idx = lane; idx < n_all * c4; idx += 32) {
+          const uint32_t r = idx / c4, c = idx - r * c4;
+          __pipeline_memcpy_async(rows + size_t(r) * s4 + c,
+                                  reinterpret_cast<const float4*>(vec_row(ix, W.all[W.order[r]])) + c, 16);
+        }
+        __pipeline_commit();
+        __pipeline_wait_prior(0);
+        __syncwarp();
+      }
+      auto ranked_row = [&](uint32_t s) -> const float* {
+        return STAGED ? reinterpret_cast<const float*>(rows + size_t(s) * s4) : vec_row(ix, W.all[W.order[s]]);
+      };
       uint32_t kept = 0;
       for (uint32_t s = 0; s < n_all && kept < R; ++s) {
         if (!W.valid[s]) continue;
-        const uint32_t pidx = W.order[s];
-        if (lane == 0) W.kept[kept] = W.all[pidx];
+        if (lane == 0) W.kept[kept] = W.all[W.order[s]];
         ++kept;
-        const float* pv = cand_row(pidx);
+        const float* pv = ranked_row(s);
         for (uint32_t i = s + 1 + lane; i < n_all; i += 32) {
           if (!W.valid[i]) continue;
-          const float d = chain_l2(pv, cand_row(W.order[i]), dim);
+          const float d = chain_l2(pv, ranked_row(i), dim);
           if (__fmul_rn(alpha, d) <= W.sd[i]) W.valid[i] = 0;
         }
         __syncwarp();
@@ -459,7 +463,7 @@ dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t
   if (r != DVS_OK) return r;
   // 3. RobustPrune of each beam into the new adjacency rows
   DVS_CUDA(cudaEventRecord(d.ins_ev[0], d.stream));
-  const size_t pstaged = size_t(Lc) * L.vec_stride * 4 + size_t(Lc) * 9 + 16;
+  const size_t pstaged = size_t(Lc) * prune_row_stride4(L.vec_stride) * 16 + size_t(Lc) * 9 + 16;
   if (pstaged <= kStageBudget) {
     if (pstaged > 48 * 1024)
       DVS_CUDA(cudaFuncSetAttribute(insert_prune_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -499,21 +503,47 @@ dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t
   DVS_CUDA(cub::DeviceRunLengthEncode::Encode(d.ins_temp, tb, keys_out, run_tg, run_cnt, nruns, int(m), d.stream));
   tb = d.ins_temp_bytes;
   DVS_CUDA(cub::DeviceScan::ExclusiveSum(d.ins_temp, tb, run_cnt, run_off, int(m) + 1, d.stream));
-  const size_t per_warp = size_t(R + 1) * L.vec_stride * 4;
   L.n = n0 + b;
-  if (per_warp <= kStageBudget) {
-    const uint32_t wpb = uint32_t(std::max<size_t>(1, std::min<size_t>(kRevWarps, kStageBudget / per_warp)));
+  {
+    // staged when a warp's candidate rows fit kRevStageMax; warps per block
+    // chosen for the most resident warps
+    const bool staged = rev_warp_bytes(R, L.vec_stride, true) <= kRevStageMax;
+    const size_t per_warp = rev_warp_bytes(R, L.vec_stride, staged);
+    int best = 0;
+    uint32_t wpb = 1, bps = 1;
+    for (uint32_t w : {1u, 2u, 4u}) {
+      const size_t smem = w * per_warp;
+      if (smem > 227 * 1024) break;
+      int nb = 0;
+      if (staged) {
+        DVS_CUDA(cudaFuncSetAttribute(reverse_edges_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(smem)));
+        DVS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, reverse_edges_kernel<true>, int(w * 32), smem));
+      } else {
+        DVS_CUDA(cudaFuncSetAttribute(reverse_edges_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      int(smem)));
+        DVS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, reverse_edges_kernel<false>, int(w * 32), smem));
+      }
+      if (int(w) * nb > best) {
+        best = int(w) * nb;
+        wpb = w;
+        bps = uint32_t(nb);
+      }
+    }
+    if (best == 0) return fail(DVS_ERR_CAPACITY, "reverse-edge warp needs more shared memory than a block has");
     const size_t smem = wpb * per_warp;
-    if (smem > 48 * 1024 - sizeof(RevWarp) * kRevWarps)
+    const uint32_t blocks = std::max(1u, std::min<uint32_t>((m + wpb - 1) / wpb, d.sm_count * bps));
+    if (staged) {
       DVS_CUDA(cudaFuncSetAttribute(reverse_edges_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(smem)));
-    const uint32_t blocks = std::min<uint32_t>((m + wpb - 1) / wpb, d.sm_count * 16);
-    reverse_edges_kernel<true><<<blocks, wpb * 32, smem, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns, alpha,
-                                                                     d.ins_stats);
-  } else {
-    const uint32_t blocks = std::min<uint32_t>((m + kRevWarps - 1) / kRevWarps, d.sm_count * 8);
-    reverse_edges_kernel<false><<<blocks, kRevWarps * 32, 0, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
-                                                                          alpha, d.ins_stats);
+      reverse_edges_kernel<true><<<blocks, wpb * 32, smem, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
+                                                                       alpha, d.ins_stats);
+    } else {
+      DVS_CUDA(cudaFuncSetAttribute(reverse_edges_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)));
+      reverse_edges_kernel<false><<<blocks, wpb * 32, smem, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
+                                                                        alpha, d.ins_stats);
+    }
   }
   DVS_CUDA(cudaGetLastError());
   DVS_CUDA(cudaEventRecord(d.ins_ev[3], d.stream));
