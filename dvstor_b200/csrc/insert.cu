@@ -79,10 +79,9 @@ constexpr uint32_t kPruneThreads = 128;
 constexpr uint32_t kRevWarps = 4;         // warps (targets in flight) per reverse-edge block
 constexpr uint32_t kMaxAll = 65;          // R + 1 candidates of an overflow prune (R <= 64)
 constexpr size_t kStageBudget = 160 * 1024;  // shared memory for staged candidate vectors per block
-// largest reverse-edge warp that stages its candidate rows (768-dim rows at
-// R = 32 still do: two warps per SM reading shared memory beat many warps
-// reading each candidate row from L2 at every greedy step)
-constexpr size_t kRevStageMax = 120 * 1024;
+// largest reverse-edge warp that stages its candidate rows; wider rows go to
+// the block-per-target kernel, which shares one staging among four warps
+constexpr size_t kRevStageMax = 32 * 1024;
 
 // rabitq_quantize_single_kernel<4,B> (src/gpu/kernels/distance_kernels.cuh:376-464)
 // on rotated rows: lane t of a quad takes dims j = t mod 4; tile sums by the
@@ -173,11 +172,11 @@ __host__ __device__ inline uint32_t prune_row_stride4(uint32_t vec_stride) { ret
 // vector v: its final beam (slots by ascending distance, from the search) is
 // the candidate list; the nearest valid candidate is kept and every later
 // valid p' with alpha * |p* - p'|^2 <= d(v, p') is dropped, until R are kept.
-// The kept slots are the new node's adjacency row (row0 + v).  STAGED: the
-// candidates' vectors are copied to shared memory once (cp.async, when Lc rows
-// fit) at an odd float4 stride, so the greedy loop reads no global memory and
-// threads reading consecutive candidates hit distinct banks.
-template <bool STAGED>
+// The kept slots are the new node's adjacency row (row0 + v).  The
+// candidates' vectors are copied to shared memory once (cp.async) at an odd
+// float4 stride, so the greedy loop reads no global memory and threads reading
+// consecutive candidates hit distinct banks.  Used when Lc rows fit; wider
+// rows go to insert_prune_passes_kernel.
 __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLayout ix, const uint32_t* __restrict__ cand,
                                                                      const float* __restrict__ cand_d,
                                                                      const uint32_t* __restrict__ counters, uint32_t Lc,
@@ -185,9 +184,9 @@ __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLa
                                                                      uint32_t* __restrict__ adj) {
   extern __shared__ __align__(16) float sm[];
   const uint32_t v = blockIdx.x, tid = threadIdx.x, R = ix.R, dim = ix.dim, vs = ix.vec_stride;
-  const uint32_t rs = 4 * prune_row_stride4(vs);             // floats between staged rows
-  float* rows = sm;                                          // STAGED: Lc candidate vectors; else p*'s vector
-  float* dd = rows + (STAGED ? size_t(Lc) * rs : vs);        // candidate distances
+  const uint32_t rs = 4 * prune_row_stride4(vs);  // floats between staged rows
+  float* rows = sm;                               // Lc candidate vectors
+  float* dd = rows + size_t(Lc) * rs;             // candidate distances
   uint32_t* sl = reinterpret_cast<uint32_t*>(dd + Lc);  // candidate slots
   uint8_t* valid = reinterpret_cast<uint8_t*>(sl + Lc);
   const uint32_t n = counters[size_t(v) * 4 + 3] & 0xFFFFu;
@@ -202,36 +201,180 @@ __global__ void __launch_bounds__(kPruneThreads) insert_prune_kernel(const DevLa
     for (uint32_t j = tid; j < R; j += blockDim.x) row[j] = j < n ? sl[j] : kEmptySlot;
     return;
   }
-  if (STAGED) {
-    const uint32_t c4 = vs >> 2;
-    for (uint32_t idx = tid; idx < n * c4; idx += blockDim.x) {
-      const uint32_t r = idx / c4, c = idx - r * c4;
-      __pipeline_memcpy_async(reinterpret_cast<float4*>(rows + size_t(r) * rs) + c,
-                              reinterpret_cast<const float4*>(vec_row(ix, sl[r])) + c, 16);
+  const uint32_t c4 = vs >> 2;
+  for (uint32_t idx = tid; idx < n * c4; idx += blockDim.x) {
+    const uint32_t r = idx / c4, c = idx - r * c4;
+    __pipeline_memcpy_async(reinterpret_cast<float4*>(rows + size_t(r) * rs) + c,
+                            reinterpret_cast<const float4*>(vec_row(ix, sl[r])) + c, 16);
+  }
+  __pipeline_commit();
+  __pipeline_wait_prior(0);
+  __syncthreads();
+  uint32_t kept = 0;  // identical in every thread
+  for (uint32_t s = 0; s < n && kept < R; ++s) {
+    if (!valid[s]) continue;
+    if (tid == 0) row[kept] = sl[s];
+    ++kept;
+    const float* pv = rows + size_t(s) * rs;
+    for (uint32_t i = s + 1 + tid; i < n; i += blockDim.x) {
+      if (!valid[i]) continue;
+      const float d = chain_l2(pv, rows + size_t(i) * rs, dim);
+      if (__fmul_rn(alpha, d) <= dd[i]) valid[i] = 0;
+    }
+    __syncthreads();
+  }
+  for (uint32_t j = kept + tid; j < R; j += blockDim.x) row[j] = kEmptySlot;
+}
+
+constexpr uint32_t kPivots = 8;  // pivot candidates per pass of insert_prune_passes_kernel
+
+// |p_k - x|^2 for the np <= kPivots pivot rows p_k (shared memory, stride vs
+// floats) against one candidate row x (global): np fma chains over dims
+// 0..dim-1 in order (each the chain of chain_l2, pivot minus candidate), the
+// candidate's chunks read once for all of them.
+__device__ __forceinline__ void chain_l2_pivots(const float* prow, uint32_t vs, uint32_t np, const float* x,
+                                                uint32_t dim, float (&out)[kPivots]) {
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const uint32_t n4 = dim >> 2, s4 = vs >> 2;
+  const float4* p4 = reinterpret_cast<const float4*>(prow);
+  float d[kPivots];
+#pragma unroll
+  for (int p = 0; p < int(kPivots); ++p) d[p] = 0.f;
+#define DVS_CHP(Y, X, D)                                   \
+  {                                                        \
+    float t = __fsub_rn(Y.x, X.x); D = __fmaf_rn(t, t, D); \
+    t = __fsub_rn(Y.y, X.y); D = __fmaf_rn(t, t, D);       \
+    t = __fsub_rn(Y.z, X.z); D = __fmaf_rn(t, t, D);       \
+    t = __fsub_rn(Y.w, X.w); D = __fmaf_rn(t, t, D);       \
+  }
+  uint32_t k4 = 0;
+  for (; k4 + 4 <= n4; k4 += 4) {
+    float4 a[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) a[c] = __ldg(x4 + k4 + c);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+      for (int p = 0; p < int(kPivots); ++p)
+        if (uint32_t(p) < np) {
+          const float4 y = p4[size_t(p) * s4 + k4 + c];
+          DVS_CHP(y, a[c], d[p])
+        }
+    }
+  }
+  for (; k4 < n4; ++k4) {
+    const float4 a = __ldg(x4 + k4);
+#pragma unroll
+    for (int p = 0; p < int(kPivots); ++p)
+      if (uint32_t(p) < np) {
+        const float4 y = p4[size_t(p) * s4 + k4];
+        DVS_CHP(y, a, d[p])
+      }
+  }
+#undef DVS_CHP
+  for (uint32_t k = n4 * 4; k < dim; ++k) {
+    const float xv = __ldg(x + k);
+#pragma unroll
+    for (int p = 0; p < int(kPivots); ++p)
+      if (uint32_t(p) < np) {
+        const float t = __fsub_rn(prow[size_t(p) * vs + k], xv);
+        d[p] = __fmaf_rn(t, t, d[p]);
+      }
+  }
+#pragma unroll
+  for (int p = 0; p < int(kPivots); ++p) out[p] = d[p];
+}
+
+// Shared memory of insert_prune_passes_kernel: kPivots pivot rows, kPivots x Lc
+// pivot distances, candidate distances and slots, pass words, valid flags.
+inline size_t prune_passes_bytes(uint32_t Lc, uint32_t vec_stride) {
+  return size_t(kPivots) * vec_stride * 4 + size_t(kPivots) * Lc * 4 + size_t(Lc) * 8 + (kPivots + 4) * 4 + Lc + 16;
+}
+
+// insert_prune_kernel for rows too wide to stage all Lc candidates: the greedy
+// pass in passes of up to kPivots pivots.  A pass takes the next kPivots valid
+// candidates (in rank order) as the pivots it may keep, stages their rows, and
+// reads each later valid candidate's row once for the distances to all of them;
+// warp 0 then walks those pivots in rank order, keeping each one still valid
+// and dropping the later candidates it prunes.  A rank skipped between two
+// pivots was invalid before the pass began, so the kept list is the one the
+// step-by-step pass gives, from the same chains, with a pass per kPivots kept
+// (or pruned) pivots instead of a read of every candidate row per kept one.
+__global__ void __launch_bounds__(kPruneThreads) insert_prune_passes_kernel(
+    const DevLayout ix, const uint32_t* __restrict__ cand, const float* __restrict__ cand_d,
+    const uint32_t* __restrict__ counters, uint32_t Lc, float alpha, uint64_t row0, uint32_t* __restrict__ adj) {
+  extern __shared__ __align__(16) float sm[];
+  const uint32_t v = blockIdx.x, tid = threadIdx.x, lane = tid & 31, R = ix.R, dim = ix.dim, vs = ix.vec_stride;
+  const uint32_t c4 = vs >> 2;
+  float* prow = sm;                                        // kPivots pivot rows
+  float* dp = prow + size_t(kPivots) * vs;                 // dp[p * Lc + i] = |pivot p - candidate i|^2
+  float* dd = dp + size_t(kPivots) * Lc;                   // candidate distances
+  uint32_t* sl = reinterpret_cast<uint32_t*>(dd + Lc);     // candidate slots
+  uint32_t* piv = sl + Lc;                                 // pivot ranks, [kPivots] count, [kPivots + 1] kept
+  uint8_t* valid = reinterpret_cast<uint8_t*>(piv + kPivots + 4);
+  const uint32_t n = counters[size_t(v) * 4 + 3] & 0xFFFFu;
+  for (uint32_t i = tid; i < n; i += blockDim.x) {
+    dd[i] = cand_d[size_t(v) * Lc + i];
+    sl[i] = cand[size_t(v) * Lc + i];
+    valid[i] = 1;
+  }
+  __syncthreads();
+  uint32_t* row = adj + (row0 + v) * R;
+  if (n <= R) {
+    for (uint32_t j = tid; j < R; j += blockDim.x) row[j] = j < n ? sl[j] : kEmptySlot;
+    return;
+  }
+  uint32_t kept = 0, cur = 0;  // identical in every thread
+  while (kept < R) {
+    if (tid < 32) {
+      uint32_t np = 0;
+      for (uint32_t b = cur; b < n && np < kPivots; b += 32) {
+        uint32_t msk = __ballot_sync(0xFFFFFFFFu, b + lane < n && valid[b + lane]);
+        while (msk && np < kPivots) {
+          if (lane == 0) piv[np] = b + __ffs(msk) - 1;
+          ++np;
+          msk &= msk - 1;
+        }
+      }
+      if (lane == 0) piv[kPivots] = np;
+    }
+    __syncthreads();
+    const uint32_t np = piv[kPivots];
+    if (np == 0) break;
+    for (uint32_t idx = tid; idx < np * c4; idx += blockDim.x) {
+      const uint32_t p = idx / c4, c = idx - p * c4;
+      __pipeline_memcpy_async(reinterpret_cast<float4*>(prow + size_t(p) * vs) + c,
+                              reinterpret_cast<const float4*>(vec_row(ix, sl[piv[p]])) + c, 16);
     }
     __pipeline_commit();
     __pipeline_wait_prior(0);
     __syncthreads();
-  }
-  uint32_t kept = 0;  // identical in every thread
-  for (uint32_t s = 0; s < n && kept < R; ++s) {
-    if (!valid[s]) continue;
-    const uint32_t pslot = sl[s];
-    if (tid == 0) row[kept] = pslot;
-    ++kept;
-    const float* pv = rows + size_t(s) * rs;
-    if (!STAGED) {
-      const float* g = vec_row(ix, pslot);
-      for (uint32_t k = tid; k < dim; k += blockDim.x) rows[k] = g[k];
-      pv = rows;
-      __syncthreads();
-    }
-    for (uint32_t i = s + 1 + tid; i < n; i += blockDim.x) {
+    for (uint32_t i = piv[0] + 1 + tid; i < n; i += blockDim.x) {
       if (!valid[i]) continue;
-      const float d = chain_l2(pv, STAGED ? rows + size_t(i) * rs : vec_row(ix, sl[i]), dim);
-      if (__fmul_rn(alpha, d) <= dd[i]) valid[i] = 0;
+      float out[kPivots];
+      chain_l2_pivots(prow, vs, np, vec_row(ix, sl[i]), dim, out);
+#pragma unroll
+      for (int p = 0; p < int(kPivots); ++p)
+        if (uint32_t(p) < np) dp[size_t(p) * Lc + i] = out[p];
     }
     __syncthreads();
+    if (tid < 32) {
+      uint32_t k2 = kept;
+      for (uint32_t p = 0; p < np && k2 < R; ++p) {
+        const uint32_t s = piv[p];
+        if (!valid[s]) continue;
+        if (lane == 0) row[k2] = sl[s];
+        ++k2;
+        for (uint32_t i = s + 1 + lane; i < n; i += 32)
+          if (valid[i] && __fmul_rn(alpha, dp[size_t(p) * Lc + i]) <= dd[i]) valid[i] = 0;
+        __syncwarp();
+      }
+      if (lane == 0) piv[kPivots + 1] = k2;
+    }
+    __syncthreads();
+    kept = piv[kPivots + 1];
+    cur = piv[np - 1] + 1;
+    __syncthreads();  // every thread has read the pass words before the next pass rewrites them
   }
   for (uint32_t j = kept + tid; j < R; j += blockDim.x) row[j] = kEmptySlot;
 }
@@ -358,6 +501,248 @@ __global__ void __launch_bounds__(kRevWarps * 32) reverse_edges_kernel(const Dev
   }
 }
 
+// l2_quad_partial2's two chains (float4 chunks t, t+4, ... then tail dim
+// n4*4 + t, diff = q - x) with plain loads, so the rows may be in shared memory.
+__device__ __forceinline__ void l2_quad2_any(const float* q, const float* xA, const float* xB, uint32_t dim,
+                                             uint32_t t, float& accA, float& accB) {
+  const uint32_t n4 = dim >> 2;
+  const float4* q4 = reinterpret_cast<const float4*>(q);
+  const float4* a4 = reinterpret_cast<const float4*>(xA);
+  const float4* b4 = reinterpret_cast<const float4*>(xB);
+  float sa = 0.f, sb = 0.f;
+  for (uint32_t i = t; i < n4; i += 4) {
+    const float4 c = q4[i], a = a4[i], b = b4[i];
+    float d;
+    d = __fsub_rn(c.x, a.x); sa = __fmaf_rn(d, d, sa);
+    d = __fsub_rn(c.x, b.x); sb = __fmaf_rn(d, d, sb);
+    d = __fsub_rn(c.y, a.y); sa = __fmaf_rn(d, d, sa);
+    d = __fsub_rn(c.y, b.y); sb = __fmaf_rn(d, d, sb);
+    d = __fsub_rn(c.z, a.z); sa = __fmaf_rn(d, d, sa);
+    d = __fsub_rn(c.z, b.z); sb = __fmaf_rn(d, d, sb);
+    d = __fsub_rn(c.w, a.w); sa = __fmaf_rn(d, d, sa);
+    d = __fsub_rn(c.w, b.w); sb = __fmaf_rn(d, d, sb);
+  }
+  const uint32_t tail = (n4 << 2) + t;
+  if (tail < dim) {
+    float d = __fsub_rn(q[tail], xA[tail]);
+    sa = __fmaf_rn(d, d, sa);
+    d = __fsub_rn(q[tail], xB[tail]);
+    sb = __fmaf_rn(d, d, sb);
+  }
+  accA = sa;
+  accB = sb;
+}
+
+// d(a, b_k), k < 4, as four fma chains over dims 0..dim-1 in order (each the
+// chain of chain_l2), interleaved; four chunks of the five rows per batch.
+// Rows are 16-byte aligned, in shared or global memory.
+__device__ __forceinline__ void chain_l2_x4(const float* a, const float* b0, const float* b1, const float* b2,
+                                            const float* b3, uint32_t dim, float (&out)[4]) {
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  const float4* bs[4] = {reinterpret_cast<const float4*>(b0), reinterpret_cast<const float4*>(b1),
+                         reinterpret_cast<const float4*>(b2), reinterpret_cast<const float4*>(b3)};
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t n4 = dim >> 2;
+  uint32_t k4 = 0;
+#define DVS_CH4(X, Y, D)                                   \
+  {                                                        \
+    float t = __fsub_rn(X.x, Y.x); D = __fmaf_rn(t, t, D); \
+    t = __fsub_rn(X.y, Y.y); D = __fmaf_rn(t, t, D);       \
+    t = __fsub_rn(X.z, Y.z); D = __fmaf_rn(t, t, D);       \
+    t = __fsub_rn(X.w, Y.w); D = __fmaf_rn(t, t, D);       \
+  }
+  for (; k4 + 4 <= n4; k4 += 4) {
+    float4 x[4], y[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      x[c] = a4[k4 + c];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) y[r][c] = bs[r][k4 + c];
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) DVS_CH4(x[c], y[r][c], d[r])
+    }
+  }
+  for (; k4 < n4; ++k4) {
+    const float4 x = a4[k4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float4 y = bs[r][k4];
+      DVS_CH4(x, y, d[r])
+    }
+  }
+#undef DVS_CH4
+  const float* bf[4] = {b0, b1, b2, b3};
+  for (uint32_t k = n4 * 4; k < dim; ++k) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float t = __fsub_rn(a[k], bf[r][k]);
+      d[r] = __fmaf_rn(t, t, d[r]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) out[r] = d[r];
+}
+
+constexpr uint32_t kRevThreads = 128;  // threads of a reverse-edge block (one target node at a time)
+
+// Pair items of n candidates: row i has (n - i + 2) / 4 (its n - 1 - i later
+// partners, four per item).
+__host__ __device__ inline uint32_t item_count(uint32_t n) {
+  uint32_t t = 0;
+  for (uint32_t i = 0; i < n; ++i) t += (n - i + 2) / 4;
+  return t;
+}
+
+// Shared memory of a reverse-edge block: its RevWarp, the (R+1)^2 pair
+// distances, the R + 1 candidate rows (index order, odd float4 stride).
+__host__ __device__ inline size_t rev_pairs_bytes(uint32_t R) { return (size_t(R + 1) * (R + 1) * 4 + 15) / 16 * 16; }
+__host__ __device__ inline size_t rev_block_bytes(uint32_t R, uint32_t vec_stride) {
+  return kRevWarpBytes + rev_pairs_bytes(R) + size_t(R + 1) * prune_row_stride4(vec_stride) * 16;
+}
+
+// reverse_edges_kernel for wide rows, where a warp's staged rows would leave
+// few warps per SM: a block of kRevThreads per target shares one staging of
+// the R + 1 candidate rows (cp.async), computes the distances to the target
+// from there, and then every pair distance of the candidates up front, four
+// chains per thread at once (thread m of row i's items takes partners
+// i+1+m + Q*q, q < 4, Q = row i's item count, so neighbouring threads read
+// neighbouring rows: no bank conflicts).  Warp 0 then runs the greedy pass on
+// those values.  Each value is the chain the step-by-step pass computes for
+// that pair (|a-b|^2 is the same chain either way round: a-b and b-a differ
+// only in sign), so the kept list is the same.
+__global__ void __launch_bounds__(kRevThreads) reverse_edges_block_kernel(const DevLayout ix, uint32_t* __restrict__ adj,
+                                                                         const uint32_t* __restrict__ targets,
+                                                                         const uint32_t* __restrict__ offs,
+                                                                         const uint32_t* __restrict__ srcs,
+                                                                         const uint32_t* __restrict__ nruns,
+                                                                         float alpha,
+                                                                         unsigned long long* __restrict__ stats) {
+  extern __shared__ __align__(16) uint8_t rev_smem[];
+  const uint32_t tid = threadIdx.x, lane = tid & 31;
+  const uint32_t R = ix.R, dim = ix.dim, c4 = ix.vec_stride >> 2, s4 = prune_row_stride4(ix.vec_stride);
+  const uint32_t n = R + 1;
+  RevWarp& B = *reinterpret_cast<RevWarp*>(rev_smem);
+  float* Dm = reinterpret_cast<float*>(rev_smem + kRevWarpBytes);
+  float4* rows = reinterpret_cast<float4*>(rev_smem + kRevWarpBytes + rev_pairs_bytes(R));
+  __shared__ uint32_t cnt_s;
+  const uint32_t ntargets = *nruns;
+  for (uint32_t w = blockIdx.x; w < ntargets; w += gridDim.x) {
+    const uint32_t tg = targets[w];
+    if (tg == kEmptySlot) continue;
+    uint32_t* row = adj + size_t(tg) * R;
+    if (tid == 0) atomicMax(stats + 3, static_cast<unsigned long long>(offs[w + 1] - offs[w]));
+    const float* tv = vec_row(ix, tg);
+    for (uint32_t e = offs[w]; e < offs[w + 1]; ++e) {
+      const uint32_t v = srcs[e];
+      if (tid < 32) {
+        const uint32_t a0 = lane < R ? row[lane] : kEmptySlot;
+        const uint32_t a1 = lane + 32 < R ? row[lane + 32] : kEmptySlot;
+        const uint32_t cnt = __popc(__ballot_sync(0xFFFFFFFFu, a0 != kEmptySlot)) +
+                             __popc(__ballot_sync(0xFFFFFFFFu, a1 != kEmptySlot));
+        if (lane < R) B.all[lane] = a0;
+        if (lane + 32 < R) B.all[lane + 32] = a1;
+        if (lane == 0) {
+          B.all[R] = v;
+          cnt_s = cnt;
+          if (cnt < R) row[cnt] = v;
+        }
+      }
+      __syncthreads();
+      const bool room = cnt_s < R;
+      __syncthreads();  // cnt_s is read by every thread before the next entry rewrites it
+      if (room) continue;
+      if (tid == 0) atomicAdd(stats + 2, 1ull);
+      for (uint32_t idx = tid; idx < n * c4; idx += kRevThreads) {
+        const uint32_t r = idx / c4, c = idx - r * c4;
+        __pipeline_memcpy_async(rows + size_t(r) * s4 + c, reinterpret_cast<const float4*>(vec_row(ix, B.all[r])) + c,
+                                16);
+      }
+      __pipeline_commit();
+      __pipeline_wait_prior(0);
+      __syncthreads();
+      auto srow = [&](uint32_t r) -> const float* { return reinterpret_cast<const float*>(rows + size_t(r) * s4); };
+      // distances to the target (batch_l2_squared_distance_kernel<4> order), two rows per lane quad
+      for (uint32_t i0 = 0; i0 < n; i0 += kRevThreads / 2) {
+        const uint32_t iA = i0 + (tid >> 2), iB = iA + kRevThreads / 4;
+        float pA = 0.f, pB = 0.f;
+        if (iA < n) l2_quad2_any(tv, srow(iA), srow(iB < n ? iB : iA), dim, tid & 3, pA, pB);
+        const float tA = quad_butterfly(pA), tB = quad_butterfly(pB);
+        if ((tid & 3) == 0) {
+          if (iA < n) B.d[iA] = tA;
+          if (iB < n) B.d[iB] = tB;
+        }
+      }
+      // every pair distance, Dm[a*n + b] = Dm[b*n + a].  Row i has
+      // (n - i + 2) / 4 items; the loops run the same trips in every thread
+      // (item k found by a scan over all rows, spare threads computing a
+      // discarded item), so a warp never splits over the long chains.
+      {
+        const uint32_t items = item_count(n);
+        for (uint32_t k0 = 0; k0 < items; k0 += kRevThreads) {
+          const uint32_t k = k0 + tid;
+          uint32_t i = 0, base = 0, acc = 0;
+          for (uint32_t r = 0; r < n; ++r) {
+            const uint32_t q = (n - r + 2) / 4;
+            if (k >= acc + q) {
+              i = r + 1;
+              base = acc + q;
+            }
+            acc += q;
+          }
+          const bool live = k < items;
+          if (!live) i = 0, base = 0;
+          const uint32_t Q = (n - i + 2) / 4, m = live ? k - base : 0;
+          const float* ri = srow(i);
+          const float* rj[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t j = i + 1 + m + Q * q;
+            rj[q] = j < n ? srow(j) : ri;
+          }
+          float dq[4];
+          __syncwarp();
+          chain_l2_x4(ri, rj[0], rj[1], rj[2], rj[3], dim, dq);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t j = i + 1 + m + Q * q;
+            if (live && j < n) {
+              Dm[i * n + j] = dq[q];
+              Dm[j * n + i] = dq[q];
+            }
+          }
+        }
+      }
+      __syncthreads();
+      if (tid < 32) {
+        for (uint32_t i = lane; i < n; i += 32) {
+          const float di = B.d[i];
+          uint32_t rk = 0;
+          for (uint32_t j = 0; j < n; ++j) rk += (B.d[j] < di) || (B.d[j] == di && j < i);
+          B.order[rk] = i;
+          B.sd[rk] = di;
+          B.valid[rk] = 1;
+        }
+        __syncwarp();
+        uint32_t kept = 0;
+        for (uint32_t s = 0; s < n && kept < R; ++s) {
+          if (!B.valid[s]) continue;
+          const uint32_t ps = B.order[s];
+          if (lane == 0) B.kept[kept] = B.all[ps];
+          ++kept;
+          for (uint32_t i = s + 1 + lane; i < n; i += 32)
+            if (B.valid[i] && __fmul_rn(alpha, Dm[ps * n + B.order[i]]) <= B.sd[i]) B.valid[i] = 0;
+          __syncwarp();
+        }
+        for (uint32_t j = lane; j < R; j += 32) row[j] = j < kept ? B.kept[j] : kEmptySlot;
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // (target, new slot) pairs of the step's new adjacency rows in insert order:
 // entry i*R + j is row i's j-th neighbour (empty slots keep the empty key).
 __global__ void edge_pairs_kernel(const uint32_t* __restrict__ rows, uint32_t m, uint32_t R, uint32_t n0,
@@ -466,16 +851,16 @@ dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t
   const size_t pstaged = size_t(Lc) * prune_row_stride4(L.vec_stride) * 16 + size_t(Lc) * 9 + 16;
   if (pstaged <= kStageBudget) {
     if (pstaged > 48 * 1024)
-      DVS_CUDA(cudaFuncSetAttribute(insert_prune_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(pstaged)));
-    insert_prune_kernel<true><<<b, kPruneThreads, pstaged, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha,
-                                                                       n0, d.adj);
+      DVS_CUDA(cudaFuncSetAttribute(insert_prune_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pstaged)));
+    insert_prune_kernel<<<b, kPruneThreads, pstaged, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha, n0,
+                                                                 d.adj);
   } else {
-    const size_t psmem = size_t(L.vec_stride) * 4 + size_t(Lc) * 9 + 16;
+    const size_t psmem = prune_passes_bytes(Lc, L.vec_stride);
+    if (psmem > 227 * 1024) return fail(DVS_ERR_CAPACITY, "prune pivots need more shared memory than a block has");
     if (psmem > 48 * 1024)
-      DVS_CUDA(cudaFuncSetAttribute(insert_prune_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      DVS_CUDA(cudaFuncSetAttribute(insert_prune_passes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(psmem)));
-    insert_prune_kernel<false><<<b, kPruneThreads, psmem, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha,
+    insert_prune_passes_kernel<<<b, kPruneThreads, psmem, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha,
                                                                       n0, d.adj);
   }
   DVS_CUDA(cudaGetLastError());
@@ -504,7 +889,18 @@ dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t
   tb = d.ins_temp_bytes;
   DVS_CUDA(cub::DeviceScan::ExclusiveSum(d.ins_temp, tb, run_cnt, run_off, int(m) + 1, d.stream));
   L.n = n0 + b;
-  {
+  if (rev_warp_bytes(R, L.vec_stride, true) > kRevStageMax && rev_block_bytes(R, L.vec_stride) <= 227 * 1024) {
+    // wide rows: a block per target shares one staging
+    const size_t smem = rev_block_bytes(R, L.vec_stride);
+    DVS_CUDA(cudaFuncSetAttribute(reverse_edges_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(smem)));
+    int bps = 0;
+    DVS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, reverse_edges_block_kernel, kRevThreads, smem));
+    if (bps == 0) return fail(DVS_ERR_CAPACITY, "reverse-edge block needs more shared memory than a block has");
+    const uint32_t blocks = std::max(1u, std::min<uint32_t>(m, d.sm_count * uint32_t(bps)));
+    reverse_edges_block_kernel<<<blocks, kRevThreads, smem, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
+                                                                        alpha, d.ins_stats);
+  } else {
     // staged when a warp's candidate rows fit kRevStageMax; warps per block
     // chosen for the most resident warps
     const bool staged = rev_warp_bytes(R, L.vec_stride, true) <= kRevStageMax;

@@ -29,14 +29,16 @@ def _assert_same_index(ix, orc):
     np.testing.assert_array_equal(adj, orc.adj[:n])
 
 
-@pytest.mark.parametrize("R,Lc,alpha,max_batch,bits,metric", [
-    (16, 64, 1.2, 256, 4, "l2"),
-    (8, 32, 1.0, 100, 4, "l2"),     # small R: most reverse edges meet full lists
-    (24, 48, 1.2, 1, 2, "l2"),      # steps of one vector: the reference's sequential insert
-    (16, 40, 1.2, 64, 8, "ip"),     # 8-bit records, IP seed distance
+@pytest.mark.parametrize("R,Lc,alpha,max_batch,bits,metric,dim", [
+    (16, 64, 1.2, 256, 4, "l2", 32),
+    (8, 32, 1.0, 100, 4, "l2", 32),     # small R: most reverse edges meet full lists
+    (24, 48, 1.2, 1, 2, "l2", 32),      # steps of one vector: the reference's sequential insert
+    (16, 40, 1.2, 64, 8, "ip", 32),     # 8-bit records, IP seed distance
+    (32, 128, 1.2, 256, 4, "l2", 384),  # wide rows: block-per-target reverse edges, prune in pivot passes
+    (48, 64, 1.2, 128, 4, "l2", 260),   # R > 32, wide rows, dim not a multiple of 8
 ])
-def test_insert_matches_oracle(gpu, oracle, tmp_path, R, Lc, alpha, max_batch, bits, metric):
-    X = normalized_gaussian(1600, 32, 41)
+def test_insert_matches_oracle(gpu, oracle, tmp_path, R, Lc, alpha, max_batch, bits, metric, dim):
+    X = normalized_gaussian(1600, dim, 41)
     n0 = 1000 if max_batch > 1 else 1400
     orc = oracle.build_index(X[:n0], R=R, L=32, bits=bits, metric=metric)
     prefix = write_oracle_index(oracle, orc, str(tmp_path / "idx"), 1)
@@ -50,7 +52,7 @@ def test_insert_matches_oracle(gpu, oracle, tmp_path, R, Lc, alpha, max_batch, b
         _assert_same_index(ix, orc)
         if R == 8:
             assert full > 0
-        Q = normalized_gaussian(120, 32, 42)
+        Q = normalized_gaussian(120, dim, 42)
         for mode in ("rabitq_gpu", "exact_gpu"):
             ids, d = ix.search(Q, 10, 48, mode)
             o_ids, o_d, _, b_ids, b_d = orc.knn(Q, 10, 48, mode, beam_cap=48 + (64 if mode == "rabitq_gpu" else 0))
