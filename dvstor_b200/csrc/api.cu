@@ -150,47 +150,67 @@ dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path) {
   return DVS_OK;
 }
 
+namespace {
+std::mutex g_shape_mu;  // guards Device::shapes
+}  // namespace
+
 dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool exact, LaunchShape& s) {
-  s.cap = cap;
-  s.cap_pad = (cap + 31) / 32 * 32;
-  if (d.lay.n < (1u << 24)) {
-    // 16-bit entries, 8 per 16-byte bucket; at least 2^(W-14) buckets for hash
-    // width W (20 bits below 2^20 nodes, else 24).  The entry limit follows
-    // slots_per_entry even where the bucket minimum is larger.
-    const uint32_t spe = slots_per_entry ? slots_per_entry
-                         : search_wide_records(exact, d.lay.code_words) ? kDefaultSlotsWide
-                                                                        : kDefaultSlots16;
-    s.vt16 = d.lay.n < (1u << 20) ? 20u : 24u;
-    s.hbuckets = std::max(1u << (s.vt16 - 14), (cap * spe + 7) / 8);
-    s.hcap = s.hbuckets * 4;
-    s.hlimit = std::min(s.hbuckets * 8, cap * spe) / 10 * 9;
-  } else {
-    const uint32_t spe = slots_per_entry ? slots_per_entry : kDefaultSlots32;
-    s.hcap = std::max(64u, (cap * spe + 31) / 32 * 32);
-    s.hlimit = s.hcap / 10 * 9;
-  }
-  const uint32_t words = search_warp_words(s.cap_pad, d.lay.vec_stride, s.hcap, d.lay.R,
-                                           search_query_layout(exact, d.lay.bits, d.lay.code_words));
-  int best_warps = 0;
-  for (uint32_t wpb : {1u, 2u, 4u, 8u}) {
-    const size_t smem = size_t(wpb) * words * 4;
-    if (smem > 227 * 1024) break;
-    int bps = 0;
-    const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, exact, wpb, smem, &bps);
-    if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
-    if (int(wpb) * bps > best_warps) {
-      best_warps = int(wpb) * bps;
-      s.wpb = wpb;
-      s.blocks_per_sm = uint32_t(bps);
+  const bool t16 = d.lay.n < (1u << 24);
+  const uint32_t vt16 = d.lay.n < (1u << 20) ? 20u : 24u;
+  const uint64_t key = uint64_t(cap) | uint64_t(slots_per_entry) << 24 | uint64_t(exact) << 40 |
+                       uint64_t(t16) << 41 | uint64_t(vt16 == 20) << 42;
+  const uint32_t qlayout = search_query_layout(exact, d.lay.bits, d.lay.code_words);
+  {
+    std::lock_guard<std::mutex> g(g_shape_mu);
+    const auto it = d.shapes.find(key);
+    if (it != d.shapes.end()) {
+      s = it->second;
+      return DVS_OK;
     }
+  }
+  // the given table size, or the largest in [kSlotsMin, kSlotsMax] that keeps
+  // the most warps resident
+  const uint32_t hi = slots_per_entry ? slots_per_entry : kSlotsMax;
+  const uint32_t lo = slots_per_entry ? slots_per_entry : kSlotsMin;
+  int best_warps = 0;
+  LaunchShape best;
+  for (uint32_t spe = hi; spe >= lo; --spe) {
+    LaunchShape c;
+    c.cap = cap;
+    c.cap_pad = (cap + 31) / 32 * 32;
+    if (t16) {
+      // 16-bit entries, 8 per 16-byte bucket; at least 2^(W-14) buckets for
+      // hash width W.  The entry limit follows spe even where the bucket
+      // minimum is larger.
+      c.vt16 = vt16;
+      c.hbuckets = std::max(1u << (vt16 - 14), (cap * spe + 7) / 8);
+      c.hcap = c.hbuckets * 4;
+      c.hlimit = std::min(c.hbuckets * 8, cap * spe) / 10 * 9;
+    } else {
+      c.hcap = std::max(64u, (cap * spe + 31) / 32 * 32);
+      c.hlimit = c.hcap / 10 * 9;
+    }
+    const uint32_t words = search_warp_words(c.cap_pad, d.lay.vec_stride, c.hcap, d.lay.R, qlayout);
+    for (uint32_t wpb : {1u, 2u, 4u, 8u}) {
+      const size_t smem = size_t(wpb) * words * 4;
+      if (smem > size_t(kMaxBlockSmem)) break;
+      int bps = 0;
+      const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, exact, wpb, smem, &bps);
+      if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
+      if (int(wpb) * bps > best_warps) {
+        best_warps = int(wpb) * bps;
+        c.wpb = wpb;
+        c.blocks_per_sm = uint32_t(bps);
+        best = c;
+      }
+    }
+    if (spe == 0) break;
   }
   if (best_warps == 0)
     return fail(DVS_ERR_CAPACITY, "beam capacity " + std::to_string(cap) + " needs more shared memory than a block has");
-  // set the attribute for the chosen configuration last
-  int bps = 0;
-  const cudaError_t e =
-      search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, exact, s.wpb, size_t(s.wpb) * words * 4, &bps);
-  if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
+  s = best;
+  std::lock_guard<std::mutex> g(g_shape_mu);
+  d.shapes[key] = best;
   return DVS_OK;
 }
 

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -32,15 +33,19 @@ void dev_free(T*& p) {
   p = nullptr;
 }
 
-// Visited-set sizing: default shared-memory slots per beam entry (32-bit table
-// for indexes of 2^24 nodes or more, compact 16-bit table below) and the spill table.
-constexpr uint32_t kDefaultSlots32 = 48;
-constexpr uint32_t kDefaultSlots16 = 48;
-// Records wider than 128 bytes: a smaller table buys resident warps (7 instead
-// of 5 per SM for 960-dim 4-bit records at beam capacity 264), and a spill
-// costs little next to estimating such records.
-constexpr uint32_t kDefaultSlotsWide = 40;
+// Visited-set sizing.  Without an explicit size the shared-memory table gets
+// between kSlotsMin and kSlotsMax slots per beam entry: the largest size that
+// keeps the most warps resident (44 for the 96-dim L = 64 search: 16 warps per
+// SM instead of 14 at 48; 40 for 960-dim records at L = 200: 7 instead of 5).
+// Queries that outgrow it spill to a per-warp table in global memory.
+constexpr uint32_t kSlotsMin = 40;
+constexpr uint32_t kSlotsMax = 48;
 constexpr uint32_t kOverflowSlots = 1u << 14;
+
+struct LaunchShape {
+  uint32_t cap = 0, cap_pad = 0, hcap = 0, wpb = 0, blocks_per_sm = 0;
+  uint32_t vt16 = 0, hbuckets = 0, hlimit = 0;
+};
 
 struct Device {
   int ordinal = 0;
@@ -79,6 +84,8 @@ struct Device {
   size_t ins_temp_bytes = 0;
   unsigned long long* ins_stats = nullptr;
   cudaEvent_t ins_ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  // launch shapes already worked out, by (capacity, slots per entry, mode, table kind)
+  std::map<uint64_t, LaunchShape> shapes;
   // kernel timing ring: (before prepare, after prepare, after search)
   static constexpr size_t kRing = 4096;
   std::vector<cudaEvent_t> tev;
@@ -118,11 +125,6 @@ struct Device {
   }
 };
 
-struct LaunchShape {
-  uint32_t cap = 0, cap_pad = 0, hcap = 0, wpb = 0, blocks_per_sm = 0;
-  uint32_t vt16 = 0, hbuckets = 0, hlimit = 0;
-};
-
 // Search-kernel launch shape for beam capacity `cap` on device `d` (exact: exact_gpu mode).
 dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool exact, LaunchShape& s);
 // Grows the device's query scratch to nq queries (and nq*k results for host calls).
@@ -141,7 +143,7 @@ struct dvs_index {
   dvs::HostIndex host;              // kept for downloads and metadata
   std::vector<dvs::Device> devs;
   uint32_t hop_limit = 0;
-  uint32_t slots_per_entry = 0;  // 0 = the default of the table kind in use
+  uint32_t slots_per_entry = 0;  // 0 = sized for the most resident warps (kSlotsMin..kSlotsMax)
   bool kernel_timing = false;
   dvs_rotation rotation = DVS_ROTATION_EXACT;
   std::mutex mu;

@@ -820,8 +820,11 @@ __global__ void l2_rows_kernel(const float* __restrict__ q, const float* __restr
 
 template <int BITS, int NPL, int RCH, bool EXACT>
 cudaError_t occ(uint32_t wpb, size_t smem, int* bps) {
+  // the largest allowance once for all shapes, so concurrent searches of other
+  // shapes never find it lowered under them
+  (void)smem;
   cudaError_t e = cudaFuncSetAttribute(search_kernel<BITS, NPL, RCH, EXACT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxBlockSmem);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(bps, search_kernel<BITS, NPL, RCH, EXACT>, int(wpb * 32),
                                                        smem);

@@ -84,6 +84,8 @@ struct SearchShape {
   uint32_t cap = 0, cap_pad = 0, hcap = 0, hlimit = 0, vt16 = 0, hbuckets = 0, wpb = 0, blocks_per_sm = 0;
 };
 
+constexpr int kMaxBlockSmem = 227 * 1024;  // dynamic shared memory a block may have on sm_100
+
 constexpr uint32_t kErrCapacity = 1u;
 constexpr uint32_t kErrHopLimit = 2u;
 constexpr uint32_t kErrTimeout = 4u;
@@ -140,7 +142,8 @@ cudaError_t launch_prepare_tc(const float* queries, uint32_t q_stride, const flo
 cudaError_t launch_search(const SearchArgs& a, uint32_t warps_per_block, uint32_t blocks, cudaStream_t stream);
 
 // Occupancy helper: blocks per SM for `warps_per_block` warps with the given
-// per-warp shared memory; also sets the kernel's dynamic smem attribute.
+// shared memory per block; also sets the kernel's dynamic shared memory
+// allowance (to kMaxBlockSmem, whatever the shape).
 cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, bool exact, uint32_t warps_per_block,
                              size_t smem_bytes, int* blocks_per_sm);
 

@@ -168,12 +168,13 @@ dvs_status dvs_set_rotation(dvs_index* index, dvs_rotation rotation);
  * DVS_ERR_HOP_LIMIT. */
 dvs_status dvs_set_hop_limit(dvs_index* index, uint32_t max_expansions);
 
-/* Shared-memory visited-set size in slots per beam entry (default 48; indexes
- * of fewer than 2^24 nodes use 16-bit entries, larger ones 32-bit).  A
- * query whose visited set outgrows it continues in a per-warp global-memory
- * table with identical results; smaller values trade shared memory (and
- * therefore more resident queries per SM) for spills.  Valid range 2..256;
- * 0 restores the default. */
+/* Shared-memory visited-set size in slots per beam entry (indexes of fewer
+ * than 2^24 nodes use 16-bit entries, larger ones 32-bit).  By default each
+ * search shape takes the largest size in 40..48 that keeps the most warps
+ * resident per SM.  A query whose visited set outgrows it continues in a
+ * per-warp global-memory table with identical results; smaller values trade
+ * shared memory (and therefore more resident queries per SM) for spills.
+ * Valid range 2..256; 0 restores the default. */
 dvs_status dvs_set_visited_slots(dvs_index* index, uint32_t slots_per_beam_entry);
 
 /* Kernel timing: when enabled, every search on a device records CUDA events
