@@ -586,7 +586,7 @@ __device__ __forceinline__ void chain_l2_x4(const float* a, const float* b0, con
   for (int r = 0; r < 4; ++r) out[r] = d[r];
 }
 
-constexpr uint32_t kRevThreads = 128;  // threads of a reverse-edge block (one target node at a time)
+constexpr uint32_t kRevThreads = 256;  // threads of a reverse-edge block (one target node at a time)
 
 // Pair items of n candidates: row i has (n - i + 2) / 4 (its n - 1 - i later
 // partners, four per item).
