@@ -533,15 +533,19 @@ __device__ __forceinline__ void l2_quad2_any(const float* q, const float* xA, co
   accB = sb;
 }
 
-// d(a, b_k), k < 4, as four fma chains over dims 0..dim-1 in order (each the
-// chain of chain_l2), interleaved; four chunks of the five rows per batch.
+// d(a, b_k), k < P, as P fma chains over dims 0..dim-1 in order (each the
+// chain of chain_l2), interleaved; four chunks of every row per batch.
 // Rows are 16-byte aligned, in shared or global memory.
-__device__ __forceinline__ void chain_l2_x4(const float* a, const float* b0, const float* b1, const float* b2,
-                                            const float* b3, uint32_t dim, float (&out)[4]) {
+template <int P>
+__device__ __forceinline__ void chain_l2_multi(const float* a, const float* const (&b)[P], uint32_t dim,
+                                               float (&out)[P]) {
   const float4* a4 = reinterpret_cast<const float4*>(a);
-  const float4* bs[4] = {reinterpret_cast<const float4*>(b0), reinterpret_cast<const float4*>(b1),
-                         reinterpret_cast<const float4*>(b2), reinterpret_cast<const float4*>(b3)};
-  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  const float4* bs[P];
+#pragma unroll
+  for (int r = 0; r < P; ++r) bs[r] = reinterpret_cast<const float4*>(b[r]);
+  float d[P];
+#pragma unroll
+  for (int r = 0; r < P; ++r) d[r] = 0.f;
   const uint32_t n4 = dim >> 2;
   uint32_t k4 = 0;
 #define DVS_CH4(X, Y, D)                                   \
@@ -552,47 +556,50 @@ __device__ __forceinline__ void chain_l2_x4(const float* a, const float* b0, con
     t = __fsub_rn(X.w, Y.w); D = __fmaf_rn(t, t, D);       \
   }
   for (; k4 + 4 <= n4; k4 += 4) {
-    float4 x[4], y[4][4];
+    float4 x[4], y[P][4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       x[c] = a4[k4 + c];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) y[r][c] = bs[r][k4 + c];
+      for (int r = 0; r < P; ++r) y[r][c] = bs[r][k4 + c];
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
 #pragma unroll
-      for (int r = 0; r < 4; ++r) DVS_CH4(x[c], y[r][c], d[r])
+      for (int r = 0; r < P; ++r) DVS_CH4(x[c], y[r][c], d[r])
     }
   }
   for (; k4 < n4; ++k4) {
     const float4 x = a4[k4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
+    for (int r = 0; r < P; ++r) {
       const float4 y = bs[r][k4];
       DVS_CH4(x, y, d[r])
     }
   }
 #undef DVS_CH4
-  const float* bf[4] = {b0, b1, b2, b3};
   for (uint32_t k = n4 * 4; k < dim; ++k) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float t = __fsub_rn(a[k], bf[r][k]);
+    for (int r = 0; r < P; ++r) {
+      const float t = __fsub_rn(a[k], b[r][k]);
       d[r] = __fmaf_rn(t, t, d[r]);
     }
   }
 #pragma unroll
-  for (int r = 0; r < 4; ++r) out[r] = d[r];
+  for (int r = 0; r < P; ++r) out[r] = d[r];
 }
 
 constexpr uint32_t kRevThreads = 256;  // threads of a reverse-edge block (one target node at a time)
+constexpr uint32_t kRevPartners = 4;   // pair distances per item (chains a thread runs at once)
 
-// Pair items of n candidates: row i has (n - i + 2) / 4 (its n - 1 - i later
-// partners, four per item).
+// Pair items of row i of n candidates: its n - 1 - i later partners,
+// kRevPartners per item.
+__host__ __device__ inline uint32_t row_items(uint32_t n, uint32_t i) {
+  return (n - 1 - i + kRevPartners - 1) / kRevPartners;
+}
 __host__ __device__ inline uint32_t item_count(uint32_t n) {
   uint32_t t = 0;
-  for (uint32_t i = 0; i < n; ++i) t += (n - i + 2) / 4;
+  for (uint32_t i = 0; i < n; ++i) t += row_items(n, i);
   return t;
 }
 
@@ -608,7 +615,7 @@ __host__ __device__ inline size_t rev_block_bytes(uint32_t R, uint32_t vec_strid
 // the R + 1 candidate rows (cp.async), computes the distances to the target
 // from there, and then every pair distance of the candidates up front, four
 // chains per thread at once (thread m of row i's items takes partners
-// i+1+m + Q*q, q < 4, Q = row i's item count, so neighbouring threads read
+// i+1+m + Q*q, q < kRevPartners, Q = row i's item count, so neighbouring threads read
 // neighbouring rows: no bank conflicts).  Warp 0 then runs the greedy pass on
 // those values.  Each value is the chain the step-by-step pass computes for
 // that pair (|a-b|^2 is the same chain either way round: a-b and b-a differ
@@ -675,17 +682,17 @@ __global__ void __launch_bounds__(kRevThreads) reverse_edges_block_kernel(const 
           if (iB < n) B.d[iB] = tB;
         }
       }
-      // every pair distance, Dm[a*n + b] = Dm[b*n + a].  Row i has
-      // (n - i + 2) / 4 items; the loops run the same trips in every thread
-      // (item k found by a scan over all rows, spare threads computing a
-      // discarded item), so a warp never splits over the long chains.
+      // every pair distance, Dm[a*n + b] = Dm[b*n + a].  The loops run the
+      // same trips in every thread (item k found by a scan over all rows,
+      // spare threads computing a discarded item), so a warp never splits
+      // over the long chains.
       {
         const uint32_t items = item_count(n);
         for (uint32_t k0 = 0; k0 < items; k0 += kRevThreads) {
           const uint32_t k = k0 + tid;
           uint32_t i = 0, base = 0, acc = 0;
           for (uint32_t r = 0; r < n; ++r) {
-            const uint32_t q = (n - r + 2) / 4;
+            const uint32_t q = row_items(n, r);
             if (k >= acc + q) {
               i = r + 1;
               base = acc + q;
@@ -694,19 +701,19 @@ __global__ void __launch_bounds__(kRevThreads) reverse_edges_block_kernel(const 
           }
           const bool live = k < items;
           if (!live) i = 0, base = 0;
-          const uint32_t Q = (n - i + 2) / 4, m = live ? k - base : 0;
+          const uint32_t Q = row_items(n, i), m = live ? k - base : 0;
           const float* ri = srow(i);
-          const float* rj[4];
+          const float* rj[kRevPartners];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < int(kRevPartners); ++q) {
             const uint32_t j = i + 1 + m + Q * q;
             rj[q] = j < n ? srow(j) : ri;
           }
-          float dq[4];
+          float dq[kRevPartners];
           __syncwarp();
-          chain_l2_x4(ri, rj[0], rj[1], rj[2], rj[3], dim, dq);
+          chain_l2_multi<kRevPartners>(ri, rj, dim, dq);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < int(kRevPartners); ++q) {
             const uint32_t j = i + 1 + m + Q * q;
             if (live && j < n) {
               Dm[i * n + j] = dq[q];

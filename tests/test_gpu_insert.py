@@ -36,6 +36,8 @@ def _assert_same_index(ix, orc):
     (16, 40, 1.2, 64, 8, "ip", 32),     # 8-bit records, IP seed distance
     (32, 128, 1.2, 256, 4, "l2", 384),  # wide rows: block-per-target reverse edges, prune in pivot passes
     (48, 64, 1.2, 128, 4, "l2", 260),   # R > 32, wide rows, dim not a multiple of 8
+    (64, 96, 1.2, 128, 4, "l2", 256),   # R = 64: 65 candidates per reverse-edge prune, pair items in rounds
+    (16, 200, 1.2, 64, 4, "l2", 288),   # L_c = 200 (the insert default): prune passes over 200 candidates
 ])
 def test_insert_matches_oracle(gpu, oracle, tmp_path, R, Lc, alpha, max_batch, bits, metric, dim):
     X = normalized_gaussian(1600, dim, 41)
