@@ -17,6 +17,13 @@ vectors) is larger than L2, which is not flushed between steps.
           over ranks).
 `--impl reference` times the reference's CPU Vamana beam search (restated in
 oracle/, the reference's own code cannot be built here) on the host cores.
+
+Other rows of the path: `--search-mode exact_gpu` (exact L2 for every
+candidate), `--bits 1|2|8` (the index built with that code width),
+`--workload` / `--n` / `--batch` / `--k` / `--beam-width` for the other
+workloads, `--placement shard` (one process, the index split over --gpus
+devices), `--mode insert|mixed` (online insert, and queries interleaved with
+inserts).
 """
 from __future__ import annotations
 
@@ -49,6 +56,9 @@ def parse_args():
     ap.add_argument("--workload", default=WORKLOAD)
     ap.add_argument("--beam-width", type=int, default=None)
     ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--search-mode", choices=["rabitq_gpu", "exact_gpu"], default="rabitq_gpu",
+                    help="exact_gpu: exact L2 for every candidate, no estimate and no rerank")
+    ap.add_argument("--bits", type=int, choices=[1, 2, 4, 8], default=4, help="RaBitQ code width of the index")
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--n", type=int, default=None, help="index size override (reduced-size runs of a workload)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU time of the cpu_baseline sample")
@@ -131,7 +141,7 @@ def workload_params(name, n=None):
 
 
 def index_prefix(args, wp):
-    tag = f"{args.workload}_n{wp['n']}_R{wp['R']}_L{wp['build_L']}_b4_s1234"
+    tag = f"{args.workload}_n{wp['n']}_R{wp['R']}_L{wp['build_L']}_b{args.bits}_s1234"
     return os.path.join(args.cache, tag, "idx")
 
 
@@ -147,8 +157,8 @@ def ensure_index(args, wp, device, dist):
         X = wp["gen"](wp["n"], wp["dim"], wp["seed"])
         log(f"[bench] generated {X.shape} in {time.time() - t:.1f}s; building index on cuda:{device}")
         t = time.time()
-        st = build_index(X, prefix, R=wp["R"], beam_width=wp["build_L"], alpha=1.2, rabitq_bits=4, seed=1234,
-                         device=device)
+        st = build_index(X, prefix, R=wp["R"], beam_width=wp["build_L"], alpha=1.2, rabitq_bits=args.bits,
+                         seed=1234, device=device)
         log(f"[bench] built in {time.time() - t:.1f}s ({st})")
         open(done, "w").write(json.dumps(st))
     dist.barrier()
@@ -238,19 +248,30 @@ def index_device_bytes(info):
     return info.num_vectors * (4 * info.R + rec + vec + 4)
 
 
-def bytes_per_query(dim, R, bits, k, H, E, Cr, nq):
+def bytes_per_query(dim, R, bits, k, H, E, Cr, nq, mode="rabitq_gpu"):
     """Algorithmic bytes of one query: query row, H adjacency rows (R ids + count),
     E RaBitQ records (codes + add + rescale), C_r rerank rows, the rotation
-    matrix amortised over the batch, and k (id, distance) results."""
+    matrix amortised over the batch, and k (id, distance) results.  exact_gpu
+    reads E full vectors instead of records and has no rerank or rotation."""
+    if mode == "exact_gpu":
+        return 4 * dim + H * (4 * R + 1) + E * 4 * dim + 8 * k
     s_code = (bits * dim + 7) // 8 + 8
     return 4 * dim + H * (4 * R + 1) + E * s_code + Cr * 4 * dim + 4 * dim * dim / nq + 8 * k
+
+
+def metric_name(k, L, mode):
+    """The headline metric; exact_gpu runs name their mode."""
+    return f"queries/sec at recall@10 parity (k={k}, L={L}{', exact_gpu' if mode == 'exact_gpu' else ''})"
+
+
+MODE_ID = {"rabitq_gpu": 0, "exact_gpu": 1}  # dvs_mode
 
 
 def profile_traffic(args, wp):
     """DRAM bytes per launch of the search kernel from the committed ncu summary,
     which covers the default workload only (None for any other configuration)."""
-    if (args.workload, wp["n"], args.batch, args.k, args.beam_width) != (
-            WORKLOAD, workload_params(WORKLOAD)["n"], BATCH, 10, None):
+    if (args.workload, wp["n"], args.batch, args.k, args.beam_width, args.search_mode, args.bits) != (
+            WORKLOAD, workload_params(WORKLOAD)["n"], BATCH, 10, None, "rabitq_gpu", 4):
         return None
     try:
         for ln in open(PROFILE_SUMMARY):
@@ -320,13 +341,13 @@ def run_reference(args):
     gt = ground_truth(idx.X, Qpool[:1000], args.k, 0)
     ids, _ = O.cpu_beam_search_batch(idx.X, idx.adj, idx.medoid, Qpool[:1000], L, args.k, threads=cores)
     line = {
-        "impl": "reference", "metric": f"queries/sec at recall@10 parity (k={args.k}, L={L})", "value": qps,
+        "impl": "reference", "metric": metric_name(args.k, L, args.search_mode), "value": qps,
         "unit": "queries/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"], "build_L": wp["build_L"],
-                   "rabitq_bits": 4, "k": args.k, "beam_width": L, "queries_per_step": per_step,
-                   "l2": "index larger than L2, not flushed"},
+                   "rabitq_bits": args.bits, "search_mode": args.search_mode, "k": args.k, "beam_width": L,
+                   "queries_per_step": per_step, "l2": "index larger than L2, not flushed"},
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port",
                          "sample": f"{per_step} queries per step, the reference's CPU beam_search restated "
                                    f"(tools/vamana_offline_builder.cc:523-625), {cores} threads"},
@@ -363,7 +384,8 @@ def run_ours(args):
     # ---- device-resident timed region ----
     with torch.cuda.stream(stream):
         for s in range(args.warmup):
-            ix.search_device(dq[s], k, L, d_out_ids=out_ids, d_out_dist=out_d, d_counters=cnt, stream=stream)
+            ix.search_device(dq[s], k, L, args.search_mode, d_out_ids=out_ids, d_out_dist=out_d, d_counters=cnt,
+                             stream=stream)
     torch.cuda.synchronize(device)
     ix.set_kernel_timing(True)
     ix.kernel_times()
@@ -374,8 +396,8 @@ def run_ours(args):
     t_wall0 = time.time()
     e0.record(stream)
     for s in range(args.steps):
-        ix.search_device(dq[args.warmup + s], k, L, d_out_ids=out_ids, d_out_dist=out_d, d_counters=cnt,
-                         stream=stream)
+        ix.search_device(dq[args.warmup + s], k, L, args.search_mode, d_out_ids=out_ids, d_out_dist=out_d,
+                         d_counters=cnt, stream=stream)
     e1.record(stream)
     torch.cuda.synchronize(device)
     t_wall1 = time.time()
@@ -390,7 +412,7 @@ def run_ours(args):
     # per-query work of the last step -> algorithmic bytes
     c = cnt.cpu().numpy().astype(np.int64)
     H, E, Cr = c[:, 0].mean(), c[:, 1].mean(), c[:, 2].mean()
-    bq = bytes_per_query(info.dim, info.R, info.rabitq_bits, k, H, E, Cr, B)
+    bq = bytes_per_query(info.dim, info.R, info.rabitq_bits, k, H, E, Cr, B, args.search_mode)
     search_avg_ms = search_ms / max(n_search, 1)
     achieved = bq * B / (search_avg_ms / 1e3) / 1e9
     peak, peak_kind = hbm_peak()
@@ -407,7 +429,8 @@ def run_ours(args):
     from dvstor_b200._lib import check, lib, ptr
 
     def host_search(s):
-        check(lib().dvs_search(ix._h, ptr(hq_all[s]), B, wp["dim"], k, L, 0, ptr(h_ids), ptr(h_d), None))
+        check(lib().dvs_search(ix._h, ptr(hq_all[s]), B, wp["dim"], k, L, MODE_ID[args.search_mode], ptr(h_ids),
+                               ptr(h_d), None))
 
     for s in range(min(args.warmup, 2)):
         host_search(s)
@@ -429,8 +452,8 @@ def run_ours(args):
         X = O.read_index(prefix) if not args.no_cpu_baseline else None
         Xv = X.X if X is not None else ix.download()[2]
         gtq = Qpool[:1000]
-        ix.search(gtq, k, L)
-        g_ids, _ = ix.search(gtq, k, L)
+        ix.search(gtq, k, L, args.search_mode)
+        g_ids, _ = ix.search(gtq, k, L, args.search_mode)
         gt = ground_truth(Xv, gtq, k, device)
         rec = recall(g_ids, gt)
         if not args.no_cpu_baseline:
@@ -440,12 +463,12 @@ def run_ours(args):
     ix.close()
     if dist.rank == 0:
         line = {
-            "metric": f"queries/sec at recall@10 parity (k={k}, L={L})", "value": value, "unit": "queries/s",
+            "metric": metric_name(k, L, args.search_mode), "value": value, "unit": "queries/s",
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"],
-                       "build_L": wp["build_L"], "rabitq_bits": 4, "k": k, "beam_width": L,
-                       "queries_per_step_per_gpu": B, "parallelism": f"replicas x{dist.world}",
+                       "build_L": wp["build_L"], "rabitq_bits": args.bits, "search_mode": args.search_mode, "k": k,
+                       "beam_width": L, "queries_per_step_per_gpu": B, "parallelism": f"replicas x{dist.world}",
                        "l2": f"index {index_device_bytes(info) / 1e9:.2f} GB larger than L2, not flushed; "
                              "fresh query batch every step"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -454,7 +477,7 @@ def run_ours(args):
                          "bytes_per_query": bq, "per_query": {"H": H, "E": E, "C_r": Cr}},
             "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": B * wp["dim"] * 4,
                     "d2h_bytes_per_step": B * k * 8},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": (1 if args.search_mode == "exact_gpu" else 2) * args.steps,
             "clocks": clocks,
             "recall_at_10": rec,
             "cpu_baseline": cpu,
@@ -494,8 +517,8 @@ def run_sharded(args):
     def step(s):
         for d in range(ngpu):
             with torch.cuda.device(d):
-                ix.search_device(dq[d][s], k, L, d_out_ids=outs[d][0], d_out_dist=outs[d][1], d_counters=outs[d][2],
-                                 stream=streams[d], device_slot=d)
+                ix.search_device(dq[d][s], k, L, args.search_mode, d_out_ids=outs[d][0], d_out_dist=outs[d][1],
+                                 d_counters=outs[d][2], stream=streams[d], device_slot=d)
 
     for s in range(args.warmup):
         step(s)
@@ -523,7 +546,7 @@ def run_sharded(args):
     value = ngpu * B * args.steps / (ms / 1e3)
     c = np.concatenate([outs[d][2].cpu().numpy() for d in range(ngpu)]).astype(np.int64)
     H, E, Cr = c[:, 0].mean(), c[:, 1].mean(), c[:, 2].mean()
-    bq = bytes_per_query(info.dim, info.R, info.rabitq_bits, k, H, E, Cr, B)
+    bq = bytes_per_query(info.dim, info.R, info.rabitq_bits, k, H, E, Cr, B, args.search_mode)
     search_avg_ms = max(st / max(n, 1) for n, _, st in ktimes)
     achieved = bq * B * ngpu / (search_avg_ms / 1e3) / 1e9
     peak, peak_kind = hbm_peak()
@@ -536,7 +559,8 @@ def run_sharded(args):
 
     def host_search(q):
         hq.numpy()[:] = q
-        check(lib().dvs_search(ix._h, ptr(hq.numpy()), B * ngpu, wp["dim"], k, L, 0, ptr(h_ids), ptr(h_d), None))
+        check(lib().dvs_search(ix._h, ptr(hq.numpy()), B * ngpu, wp["dim"], k, L, MODE_ID[args.search_mode],
+                               ptr(h_ids), ptr(h_d), None))
 
     host_search(per[0].reshape(-1, wp["dim"]))
     t = time.perf_counter()
@@ -545,17 +569,17 @@ def run_sharded(args):
     e2e = ngpu * B * args.steps / (time.perf_counter() - t)
 
     gtq = Qpool[:1000]
-    g_ids, _ = ix.search(gtq, k, L)
+    g_ids, _ = ix.search(gtq, k, L, args.search_mode)
     Xv = ix.download()[2]
     rec = recall(g_ids, ground_truth(Xv, gtq, k, 0))
     ix.close()
     line = {
-        "metric": f"queries/sec at recall@10 parity (k={k}, L={L})", "value": value, "unit": "queries/s",
+        "metric": metric_name(k, L, args.search_mode), "value": value, "unit": "queries/s",
         "n_gpus": ngpu, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"], "build_L": wp["build_L"],
-                   "rabitq_bits": 4, "k": k, "beam_width": L, "queries_per_step_per_gpu": B,
-                   "parallelism": f"shard x{ngpu} (one process, peer HBM reads)",
+                   "rabitq_bits": args.bits, "search_mode": args.search_mode, "k": k, "beam_width": L,
+                   "queries_per_step_per_gpu": B, "parallelism": f"shard x{ngpu} (one process, peer HBM reads)",
                    "l2": f"index {index_device_bytes(info) / 1e9:.2f} GB split over {ngpu} GPUs, not flushed"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * ngpu, "unit": "GB/s",
                      "frac": achieved / (peak * ngpu), "traffic": None,
@@ -563,7 +587,7 @@ def run_sharded(args):
                      "kernel_ms": search_avg_ms, "bytes_per_query": bq, "per_query": {"H": H, "E": E, "C_r": Cr}},
         "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": B * ngpu * wp["dim"] * 4,
                 "d2h_bytes_per_step": B * ngpu * k * 8},
-        "gpu_launches": 2 * args.steps * ngpu,
+        "gpu_launches": (1 if args.search_mode == "exact_gpu" else 2) * args.steps * ngpu,
         "clocks": clocks,
         "recall_at_10": rec,
         "cpu_baseline": None,
@@ -630,7 +654,7 @@ def run_insert(args):
         "metric": f"inserts/sec (L_c={Lc}, alpha={args.alpha})", "value": value, "unit": "inserts/s",
         "n_gpus": 1, "steps": stats["steps"], "warmup": args.warmup, "ms_per_step": 1e3 * el / max(stats["steps"], 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "n_base": n0, "dim": wp["dim"], "R": wp["R"], "rabitq_bits": 4,
+        "config": {"workload": args.workload, "n_base": n0, "dim": wp["dim"], "R": wp["R"], "rabitq_bits": args.bits,
                    "inserted": total, "insert_batch": B, "beam_width_construction": Lc, "alpha": args.alpha},
         "e2e": {"value": value, "unit": "inserts/s", "h2d_bytes_per_step": B * wp["dim"] * 4 + B * 4,
                 "d2h_bytes_per_step": B * wp["R"] * 4},
@@ -694,7 +718,7 @@ def run_mixed(args):
         "value": ops / el, "unit": "ops/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "n_base": n0, "dim": wp["dim"], "R": wp["R"], "rabitq_bits": 4,
+        "config": {"workload": args.workload, "n_base": n0, "dim": wp["dim"], "R": wp["R"], "rabitq_bits": args.bits,
                    "queries_per_step": Bq, "inserts_per_step": Bi, "metric": "l2 (normalised vectors: the same "
                    "ranking as ip; estimates and rerank are L2 in both reference modes)"},
         "queries_per_s": Bq * args.steps / el, "inserts_per_s": Bi * args.steps / el,
