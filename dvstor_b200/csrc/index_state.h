@@ -35,8 +35,8 @@ void dev_free(T*& p) {
 
 // Visited-set sizing.  Without an explicit size the shared-memory table gets
 // between kSlotsMin and kSlotsMax slots per beam entry: the largest size that
-// keeps the most warps resident (44 for the 96-dim L = 64 search: 16 warps per
-// SM instead of 14 at 48; 40 for 960-dim records at L = 200: 7 instead of 5).
+// keeps the most warps resident (48 for the 96-dim L = 64 search, 16 warps per
+// SM; 40 for 960-dim records at L = 200: 7 warps instead of 5).
 // Queries that outgrow it spill to a per-warp table in global memory.
 constexpr uint32_t kSlotsMin = 40;
 constexpr uint32_t kSlotsMax = 48;

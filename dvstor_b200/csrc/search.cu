@@ -387,15 +387,13 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
   const DevLayout& ix = a.ix;
   constexpr uint32_t qlayout = EXACT ? kQueryRaw : (RCH == 0 && BITS != 8 ? kQueryChain : kQueryRot);
   uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R, qlayout);
-  float* bdA = reinterpret_cast<float*>(base);
-  uint32_t* biA = base + a.cap_pad;
-  float* bdB = reinterpret_cast<float*>(base + 2 * a.cap_pad);
-  uint32_t* biB = base + 3 * a.cap_pad;
+  float* bd = reinterpret_cast<float*>(base);  // the beam: distances
+  uint32_t* bi = base + a.cap_pad;            // and slot | expanded bit
   // exact_gpu: the query (qv); rabitq_gpu: q' (qr) in dimension or chain order
-  float* qv = reinterpret_cast<float*>(base + 4 * a.cap_pad);
+  float* qv = reinterpret_cast<float*>(base + 2 * a.cap_pad);
   float* qr = qv;
   const uint32_t cs = chain_stride(a.dim_pad);
-  uint32_t* cid = base + 4 * a.cap_pad + (qlayout == kQueryChain ? 4 * cs : a.dim_pad);
+  uint32_t* cid = base + 2 * a.cap_pad + (qlayout == kQueryChain ? 4 * cs : a.dim_pad);
   float* cd = reinterpret_cast<float*>(cid + 32 * NPL);
   float* sd = reinterpret_cast<float*>(cid + 64 * NPL);
   uint32_t* sid = cid + 96 * NPL;
@@ -440,17 +438,13 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
     __syncwarp();
     const float md = seed_distance_warp(rabitq ? qg : qv, vec_row(ix, ix.medoid), dim, ix.metric == 1, lane);
     if (lane == 0) {
-      bdA[0] = md;
-      biA[0] = ix.medoid;
+      bd[0] = md;
+      bi[0] = ix.medoid;
       if (!a.vt16) htab[4 * hash_slot(ix.medoid, a.hcap >> 2)] = ix.medoid;
     }
     __syncwarp();
     if (a.vt16 && lane == 0) visit16(htab, a.hbuckets, a.inv_hbuckets, ix.medoid, true, a.vt16);
     __syncwarp();
-    float* bd = bdA;
-    uint32_t* bi = biA;
-    float* bdo = bdB;
-    uint32_t* bio = biB;
     uint32_t nb = 1, hcount = 1, gcount = 0, H = 0, E = 0, err = 0, scan_from = 0;
     if (nonfinite) {
       nb = 0;  // nothing is selectable: the loop ends at once and every result slot is empty
@@ -657,17 +651,8 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       }
       uint32_t first_pos = 0xFFFFFFFFu;
 #pragma unroll
-      for (int h = 0; h < NPL; ++h) {
-        const uint32_t i = 32u * h + lane;
-        if (i < ms) {
-          const uint32_t pos = rank[h] + ins[h];
-          first_pos = min(first_pos, pos);
-          if (pos < a.cap) {
-            bdo[pos] = nd[h];
-            bio[pos] = nid[h];
-          }
-        }
-      }
+      for (int h = 0; h < NPL; ++h)
+        if (32u * h + lane < ms) first_pos = min(first_pos, rank[h] + ins[h]);
       first_pos = __reduce_min_sync(kFull, first_pos);
       // beam entry p moves down by #{survivors with ins <= p}.  ins depends on
       // the distance alone, so in rank order it never decreases: the count is
@@ -679,32 +664,51 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       for (int h = 0; h < NPL; ++h)
         if (32u * h + lane < ms) sins[rank[h]] = ins[h];
       __syncwarp();
-      for (uint32_t p0 = 0; p0 < nb; p0 += 32) {
+      // The beam moves in place, from its last 32-entry chunk down to the chunk
+      // of the first insertion point (entries before it do not move): every
+      // lane of a chunk reads its entry before any lane writes, and an entry
+      // lands at or after its own position, in chunks already read.
+      const uint32_t low_chunk = sins[0] & ~31u;
+      for (uint32_t p0 = (nb - 1) & ~31u;; p0 -= 32) {
         const uint32_t p = p0 + lane;
-        uint32_t lo = 0, hi = ms;
-        while (lo < hi) {
-          const uint32_t mid = (lo + hi) >> 1;
-          if (sins[mid] <= p)
-            lo = mid + 1;
-          else
-            hi = mid;
+        uint32_t shift = 0;
+        float dv = 0.f;
+        uint32_t iv = 0;
+        if (p < nb) {
+          uint32_t lo = 0, hi = ms;
+          while (lo < hi) {
+            const uint32_t mid = (lo + hi) >> 1;
+            if (sins[mid] <= p)
+              lo = mid + 1;
+            else
+              hi = mid;
+          }
+          shift = lo;
+          dv = bd[p];
+          iv = bi[p];
         }
-        const uint32_t shift = lo;
-        if (p < nb && p + shift < a.cap) {
-          bdo[p + shift] = bd[p];
-          bio[p + shift] = bi[p];
+        __syncwarp();
+        if (shift && p + shift < a.cap) {
+          bd[p + shift] = dv;
+          bi[p + shift] = iv;
+        }
+        __syncwarp();
+        if (p0 <= low_chunk) break;
+      }
+      // the survivors fill the positions the moves left
+#pragma unroll
+      for (int h = 0; h < NPL; ++h) {
+        if (32u * h + lane < ms) {
+          const uint32_t pos = rank[h] + ins[h];
+          if (pos < a.cap) {
+            bd[pos] = nd[h];
+            bi[pos] = nid[h];
+          }
         }
       }
       scan_from = min(first_pos, uint32_t(best) + 1);
-      const uint32_t nb_new = min(a.cap, nb + ms);
+      nb = min(a.cap, nb + ms);
       __syncwarp();
-      float* tf = bd;
-      bd = bdo;
-      bdo = tf;
-      uint32_t* ti = bi;
-      bi = bio;
-      bio = ti;
-      nb = nb_new;
     }
 
     // ---- rerank (vamana.hh:358-422) and final order (vamana.hh:424-446) ----

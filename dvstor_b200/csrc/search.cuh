@@ -108,8 +108,8 @@ constexpr uint32_t kQueryRaw = 0, kQueryRot = 1, kQueryChain = 2;
 // position fall in four distinct bank groups.
 __host__ __device__ inline uint32_t chain_stride(uint32_t dim_pad) { return ((dim_pad / 4 + 3) & ~7u) + 4; }
 
-// Words of shared memory one warp of the search kernel uses: two beams (cap_pad
-// distances + ids each), the query in the given layout, four candidate staging
+// Words of shared memory one warp of the search kernel uses: the beam (cap_pad
+// distances + ids), the query in the given layout, four candidate staging
 // arrays of 32 x slots-per-lane entries (slots per lane = 2 when R > 32, else
 // 1), the visited table (at least dim_pad words in the rabitq layouts, which
 // put the query there for the rerank).  Every part is a multiple of 4 words, so
@@ -118,7 +118,7 @@ __host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t
                                                       uint32_t qlayout) {
   const uint32_t qwords = qlayout == kQueryChain ? 4 * chain_stride(dim_pad) : dim_pad;
   const uint32_t twords = qlayout == kQueryRaw ? hcap : (hcap > dim_pad ? hcap : dim_pad);
-  return 4 * cap_pad + qwords + (R > 32 ? 256 : 128) + twords;
+  return 2 * cap_pad + qwords + (R > 32 ? 256 : 128) + twords;
 }
 
 // q' = P^T q (the sequential fmaf chain over i per output) and the query
