@@ -208,87 +208,87 @@ __device__ __forceinline__ void code_word(uint32_t word, uint32_t wi, int e, con
   }
 }
 
-// Chain t of two records' estimates (ids cA and cB; cB may repeat cA when the
-// round has no second record), computed by lane t of a lane quad: the
-// reference kernel's own tile-of-4 split (lane t sums dims j = t mod 4 for B in
-// {1,2,4}, char4 steps c = t mod 4 for B = 8), each chain in ascending order.
-// Used for records wider than 128 bytes.  The two chains are independent, so
-// their loads and FMAs interleave; each q' read serves both.  For B in {1,2,4}
-// `q` is this lane's chain of the chain-major q' (position p = dim 4p + t), for
-// B = 8 the dimension-order q'.  Lane 0 also returns the records' add and
-// rescale factors.
-template <int BITS>
-__device__ __forceinline__ void estimate_quad_chain2(const DevLayout& ix, uint32_t cA, uint32_t cB,
-                                                     const float* __restrict__ q, uint32_t t, float& sA, float& sB,
-                                                     float (&fA)[2], float (&fB)[2]) {
-  const uint32_t* rA = reinterpret_cast<const uint32_t*>(rec_row(ix, cA));
-  const uint32_t* rB = reinterpret_cast<const uint32_t*>(rec_row(ix, cB));
-  if (t == 0) {
-    fA[0] = __uint_as_float(__ldg(rA + ix.code_words));
-    fA[1] = __uint_as_float(__ldg(rA + ix.code_words + 1));
-    fB[0] = __uint_as_float(__ldg(rB + ix.code_words));
-    fB[1] = __uint_as_float(__ldg(rB + ix.code_words + 1));
-  }
-  sA = 0.f;
-  sB = 0.f;
-  if constexpr (BITS == 8) {
-    // lane t takes words t, t+4, ...: 8 of each record in flight per batch
-    const uint32_t nw = ix.dim >> 2;
-    for (uint32_t w0 = t; w0 < nw; w0 += 32) {
-      uint32_t a[8], b[8];
+// Chain t of NR records' estimates (ids c[r]; a record may repeat c[0] when
+// the round has fewer), computed by lane t of a lane quad: the reference
+// kernel's own tile-of-4 split (lane t sums dims j = t mod 4 for B in {1,2,4},
+// char4 steps c = t mod 4 for B = 8), each chain in ascending order.  Used for
+// records wider than 128 bytes.  The NR chains are independent, so their
+// loads and FMAs interleave; each q' read serves all of them; KB chunks of
+// every record are in flight per batch.  For B in {1,2,4} `q` is this lane's
+// chain of the chain-major q' (position p = dim 4p + t), for B = 8 the
+// dimension-order q'.  Lane 0 also returns the records' add and rescale
+// factors.
+template <int BITS, int NR, int KB>
+__device__ __forceinline__ void estimate_quad_chains(const DevLayout& ix, const uint32_t (&c)[NR],
+                                                     const float* __restrict__ q, uint32_t t, float (&s)[NR],
+                                                     float (&f)[NR][2]) {
+  const uint32_t* r[NR];
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (w0 + 4 * k < nw) {
-          a[k] = __ldg(rA + w0 + 4 * k);
-          b[k] = __ldg(rB + w0 + 4 * k);
+  for (int k = 0; k < NR; ++k) {
+    r[k] = reinterpret_cast<const uint32_t*>(rec_row(ix, c[k]));
+    s[k] = 0.f;
+    if (t == 0) {
+      f[k][0] = __uint_as_float(__ldg(r[k] + ix.code_words));
+      f[k][1] = __uint_as_float(__ldg(r[k] + ix.code_words + 1));
+    }
+  }
+  if constexpr (BITS == 8) {
+    // lane t takes words t, t+4, ...: KB of each record in flight per batch
+    const uint32_t nw = ix.dim >> 2;
+    for (uint32_t w0 = t; w0 < nw; w0 += 4 * KB) {
+      uint32_t a[NR][KB];
+#pragma unroll
+      for (int j = 0; j < KB; ++j)
+        if (w0 + 4 * j < nw) {
+#pragma unroll
+          for (int k = 0; k < NR; ++k) a[k][j] = __ldg(r[k] + w0 + 4 * j);
         }
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (w0 + 4 * k < nw) {
-          const float4 q4 = *reinterpret_cast<const float4*>(q + 4 * (w0 + 4 * k));
-          sA = __fadd_rn(sA, rabitq_char4(a[k], q4));
-          sB = __fadd_rn(sB, rabitq_char4(b[k], q4));
+      for (int j = 0; j < KB; ++j)
+        if (w0 + 4 * j < nw) {
+          const float4 q4 = *reinterpret_cast<const float4*>(q + 4 * (w0 + 4 * j));
+#pragma unroll
+          for (int k = 0; k < NR; ++k) s[k] = __fadd_rn(s[k], rabitq_char4(a[k][j], q4));
         }
     }
   } else {
     // a 16-byte chunk holds kPer = 32/B dims of each of the 4 chains: positions
     // kPer*ch .. kPer*ch + kPer-1 of this lane's chain, word e giving kPer/4 of them
     constexpr uint32_t kPer = 32 / BITS, kMask = (1u << BITS) - 1u;
-    const uint4* a4 = reinterpret_cast<const uint4*>(rA);
-    const uint4* b4 = reinterpret_cast<const uint4*>(rB);
     const uint32_t nch = (ix.dim / kPer) >> 2;  // chunks whose every dim is < dim
     const uint32_t sh0 = BITS * t;
-    for (uint32_t ch = 0; ch < nch; ch += 8) {
-      uint4 va[8], vb[8];
+    for (uint32_t ch = 0; ch < nch; ch += KB) {
+      uint4 v[NR][KB];
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (ch + k < nch) {
-          va[k] = __ldg(a4 + ch + k);
-          vb[k] = __ldg(b4 + ch + k);
+      for (int j = 0; j < KB; ++j)
+        if (ch + j < nch) {
+#pragma unroll
+          for (int k = 0; k < NR; ++k) v[k][j] = __ldg(reinterpret_cast<const uint4*>(r[k]) + ch + j);
         }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (ch + k < nch) {
+      for (int j = 0; j < KB; ++j) {
+        if (ch + j < nch) {
           float qf[kPer];
-          const float4* q4 = reinterpret_cast<const float4*>(q + (ch + k) * kPer);
+          const float4* q4 = reinterpret_cast<const float4*>(q + (ch + j) * kPer);
 #pragma unroll
           for (uint32_t g = 0; g < kPer / 4; ++g) {
-            const float4 f = q4[g];
-            qf[4 * g] = f.x;
-            qf[4 * g + 1] = f.y;
-            qf[4 * g + 2] = f.z;
-            qf[4 * g + 3] = f.w;
+            const float4 fq = q4[g];
+            qf[4 * g] = fq.x;
+            qf[4 * g + 1] = fq.y;
+            qf[4 * g + 2] = fq.z;
+            qf[4 * g + 3] = fq.w;
           }
-          const uint32_t wa[4] = {va[k].x, va[k].y, va[k].z, va[k].w};
-          const uint32_t wb[4] = {vb[k].x, vb[k].y, vb[k].z, vb[k].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
 #pragma unroll
             for (uint32_t i = 0; i < kPer / 4; ++i) {
               const uint32_t sh = sh0 + 4 * BITS * i;
               const float qv = qf[e * (kPer / 4) + i];
-              sA = __fmaf_rn(small_u2f((wa[e] >> sh) & kMask), qv, sA);
-              sB = __fmaf_rn(small_u2f((wb[e] >> sh) & kMask), qv, sB);
+#pragma unroll
+              for (int k = 0; k < NR; ++k) {
+                const uint32_t w = e == 0 ? v[k][j].x : e == 1 ? v[k][j].y : e == 2 ? v[k][j].z : v[k][j].w;
+                s[k] = __fmaf_rn(small_u2f((w >> sh) & kMask), qv, s[k]);
+              }
             }
           }
         }
@@ -296,12 +296,14 @@ __device__ __forceinline__ void estimate_quad_chain2(const DevLayout& ix, uint32
     }
     // words past the last whole chunk, the partial last word included
     for (uint32_t wi = nch * 4; wi * kPer < ix.dim; ++wi) {
-      const uint32_t wa = __ldg(rA + wi), wb = __ldg(rB + wi);
+      uint32_t w[NR];
+#pragma unroll
+      for (int k = 0; k < NR; ++k) w[k] = __ldg(r[k] + wi);
       const uint32_t j0 = wi * kPer;
       for (uint32_t n = t; n < kPer && j0 + n < ix.dim; n += 4) {
         const float qv = q[(j0 + n) >> 2];
-        sA = __fmaf_rn(small_u2f((wa >> (BITS * n)) & kMask), qv, sA);
-        sB = __fmaf_rn(small_u2f((wb >> (BITS * n)) & kMask), qv, sB);
+#pragma unroll
+        for (int k = 0; k < NR; ++k) s[k] = __fmaf_rn(small_u2f((w[k] >> (BITS * n)) & kMask), qv, s[k]);
       }
     }
   }
@@ -364,6 +366,10 @@ __device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n,
   }
   return lo;
 }
+
+// Wide records: records per lane quad per round and 16-byte chunks of each in
+// flight per batch.
+constexpr int kWideRecs = 3, kWideBatch = 6;
 
 // Register cap of a search_kernel instantiation.  R <= 32 with records held in
 // registers: 128, four warps per SM sub-partition (16,384 registers each), so
@@ -584,22 +590,29 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       if (!rabitq) {
         l2_rows_warp(ix, qv, cid, m, cd, lane, 0xFFFFFFFFu);
       } else if (RCH == 0) {
-        // wide records: 16 per round, two per lane quad (candidates i and
-        // i + 8), chains reduced with the tile butterfly
+        // wide records: 8 * kWideRecs per round, kWideRecs per lane quad
+        // (candidates i, i + 8, ...), chains reduced with the tile butterfly
         const uint32_t t = lane & 3;
         const float* qt = qlayout == kQueryChain ? qr + t * cs : qr;
-        for (uint32_t i0 = 0; i0 < m; i0 += 16) {
-          const uint32_t iA = i0 + (lane >> 2), iB = iA + 8;
-          float pA = 0.f, pB = 0.f, fA[2] = {0.f, 0.f}, fB[2] = {0.f, 0.f};
-          if (iA < m) {
-            const uint32_t cA = cid[iA];
-            estimate_quad_chain2<BITS>(ix, cA, iB < m ? cid[iB] : cA, qt, t, pA, pB, fA, fB);
+        for (uint32_t i0 = 0; i0 < m; i0 += 8 * kWideRecs) {
+          const uint32_t i = i0 + (lane >> 2);
+          float p[kWideRecs], f[kWideRecs][2];
+#pragma unroll
+          for (int k = 0; k < kWideRecs; ++k) {
+            p[k] = 0.f;
+            f[k][0] = f[k][1] = 0.f;
           }
-          const float dA = quad_butterfly(pA), dB = quad_butterfly(pB);
-          if (t == 0) {
-            const float top = float((1u << BITS) - 1u);
-            if (iA < m) cd[iA] = rabitq_finish(dA, fA[0], fA[1], q_add, q_k1, top);
-            if (iB < m) cd[iB] = rabitq_finish(dB, fB[0], fB[1], q_add, q_k1, top);
+          if (i < m) {
+            uint32_t c[kWideRecs];
+#pragma unroll
+            for (int k = 0; k < kWideRecs; ++k) c[k] = i + 8u * k < m ? cid[i + 8u * k] : cid[i];
+            estimate_quad_chains<BITS, kWideRecs, kWideBatch>(ix, c, qt, t, p, f);
+          }
+#pragma unroll
+          for (int k = 0; k < kWideRecs; ++k) {
+            const float d = quad_butterfly(p[k]);
+            if (t == 0 && i + 8u * k < m)
+              cd[i + 8u * k] = rabitq_finish(d, f[k][0], f[k][1], q_add, q_k1, float((1u << BITS) - 1u));
           }
         }
       }
