@@ -72,6 +72,9 @@ def parse_args():
     ap.add_argument("--alpha", type=float, default=1.2)
     ap.add_argument("--placement", choices=["replicate", "shard"], default="replicate",
                     help="shard: one process over --gpus devices, the index split by slot (run without torchrun)")
+    ap.add_argument("--parity-queries", type=int, default=500,
+                    help="queries of the workload checked against the oracle's Vamana::knn after the timed region")
+    ap.add_argument("--build-index-only", action="store_true", help=argparse.SUPPRESS)
     return ap.parse_args()
 
 
@@ -145,14 +148,21 @@ def index_prefix(args, wp):
     return os.path.join(args.cache, tag, "idx")
 
 
-def ensure_index(args, wp, device, dist):
-    """Builds the index once per box (GPU builder) into the cache directory."""
-    from dvstor_b200 import datasets
-    from dvstor_b200.builder import build_index
-
+def ensure_index(args, wp, device, dist, subprocess_build=False):
+    """Builds the index once per box (GPU builder) into the cache directory.
+    subprocess_build: build in a child process, so this process never loads
+    the library (the reference arm)."""
     prefix = index_prefix(args, wp)
     done = prefix + ".done"
+    if dist.local == 0 and not os.path.exists(done) and subprocess_build:
+        cmd = [sys.executable, os.path.abspath(__file__), "--build-index-only", "--workload", args.workload,
+               "--bits", str(args.bits), "--cache", args.cache]
+        if args.n:
+            cmd += ["--n", str(args.n)]
+        subprocess.run(cmd, check=True, stdout=sys.stderr)
     if dist.local == 0 and not os.path.exists(done):
+        from dvstor_b200.builder import build_index
+
         t = time.time()
         X = wp["gen"](wp["n"], wp["dim"], wp["seed"])
         log(f"[bench] generated {X.shape} in {time.time() - t:.1f}s; building index on cuda:{device}")
@@ -241,6 +251,45 @@ def recall(ids, gt):
     return float(np.mean([len(set(ids[i][:k].tolist()) & set(gt[i].tolist())) / k for i in range(len(gt))]))
 
 
+def parity_check(ix, orc, Q, k, L, mode, device):
+    """The GPU search against the oracle's Vamana::knn (src/vamana/vamana.hh:57-452)
+    on the same index files and queries: a query matches when its distances are
+    equal bit for bit, its expansions H, estimates E and reranked rows C_r are
+    equal, and its ids are equal except inside groups of exactly equal final
+    distance (std::sort leaves their order unspecified)."""
+    import torch
+
+    nq = Q.shape[0]
+    dev = f"cuda:{device}"
+    dq = torch.from_numpy(np.ascontiguousarray(Q)).to(dev)
+    ids_t = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    d_t = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    c_t = torch.zeros((nq, 4), dtype=torch.int32, device=dev)
+    ix.search_device(dq, k, L, mode, d_out_ids=ids_t, d_out_dist=d_t, d_counters=c_t)
+    torch.cuda.synchronize(device)
+    g_ids = ids_t.cpu().numpy().view(np.uint32)
+    g_d = d_t.cpu().numpy()
+    g_c = c_t.cpu().numpy().view(np.uint32)
+    cap = L + 64 if mode == "rabitq_gpu" else L
+    t = time.perf_counter()
+    o_ids, o_d, o_c, b_ids, b_d = orc.knn(Q, k, L, mode, beam_cap=cap, threads=os.cpu_count() or 1)
+    oracle_s = time.perf_counter() - t
+    mism, ties = 0, 0
+    for q in range(nq):
+        ok = np.array_equal(g_d[q].view(np.uint32), o_d[q].view(np.uint32)) and np.array_equal(g_c[q, :3], o_c[q, :3])
+        if ok:
+            for i in np.nonzero(g_ids[q] != o_ids[q])[0]:
+                dv = g_d[q, i]
+                tie = (g_d[q] == dv).sum() > 1 or (b_d[q] == dv).sum() > 1
+                if tie and int(g_ids[q, i]) in set(b_ids[q][b_d[q] == dv].tolist()):
+                    ties += 1
+                else:
+                    ok = False
+        mism += 0 if ok else 1
+    return {"queries": nq, "mismatches": mism, "tie_diffs": ties, "oracle_s": round(oracle_s, 2),
+            "rule": "distances and H/E/C_r equal bit for bit, ids equal outside exact-distance ties"}
+
+
 def index_device_bytes(info):
     """HBM bytes of one replica: adjacency, records (16-byte padded), vectors, ids."""
     rec = (((info.rabitq_bits * info.dim + 7) // 8 + 3) // 4 * 4 + 8 + 15) // 16 * 16
@@ -267,19 +316,41 @@ def metric_name(k, L, mode):
 MODE_ID = {"rabitq_gpu": 0, "exact_gpu": 1}  # dvs_mode
 
 
+KERNEL_SOURCES = ("search.cu", "search.cuh", "device_math.cuh", "api.cu", "index_state.h")
+
+
+def kernel_sources_digest() -> str:
+    """sha256 (first 16 hex digits) of the sources that decide what the search
+    kernel reads and writes: the kernel, its launch shape and its scratch."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for f in KERNEL_SOURCES:
+        h.update(open(os.path.join(ROOT, "dvstor_b200", "csrc", f), "rb").read())
+    return h.hexdigest()[:16]
+
+
 def profile_traffic(args, wp):
-    """DRAM bytes per launch of the search kernel from the committed ncu summary,
-    which covers the default workload only (None for any other configuration)."""
+    """DRAM bytes per launch of the search kernel from the committed ncu summary:
+    (bytes, provenance).  The summary covers the default workload only and names
+    the digest of the kernel sources it was captured from; for any other
+    configuration, or when the sources have changed since, bytes is None."""
     if (args.workload, wp["n"], args.batch, args.k, args.beam_width, args.search_mode, args.bits) != (
             WORKLOAD, workload_params(WORKLOAD)["n"], BATCH, 10, None, "rabitq_gpu", 4):
-        return None
+        return None, "no ncu capture of this configuration"
+    tr, digest = None, None
     try:
         for ln in open(PROFILE_SUMMARY):
             if ln.startswith("traffic_bytes_per_launch_full_workload="):
-                return float(ln.split("=", 1)[1].split()[0])
+                tr = float(ln.split("=", 1)[1].split()[0])
+            if ln.startswith("kernel_sources_sha256_16="):
+                digest = ln.split("=", 1)[1].split()[0]
     except OSError:
-        pass
-    return None
+        return None, "no ncu summary"
+    src = f"ncu capture in profiles/{os.path.basename(PROFILE_SUMMARY)} (kernel sources {digest})"
+    if tr is None or digest != kernel_sources_digest():
+        return None, src + f" does not match the current kernel sources ({kernel_sources_digest()})"
+    return tr, src
 
 
 def hbm_peak():
@@ -321,7 +392,7 @@ def run_reference(args):
     L = args.beam_width or wp["search_L"]
     dist_single = Dist.__new__(Dist)
     dist_single.world, dist_single.rank, dist_single.local, dist_single.pg = 1, 0, 0, None
-    prefix = ensure_index(args, wp, 0, dist_single)
+    prefix = ensure_index(args, wp, 0, dist_single, subprocess_build=True)
     idx = O.read_index(prefix)
     cores = os.cpu_count() or 1
     Qpool = datasets.queries_for(args.workload, 200_000, stream=0)
@@ -416,7 +487,8 @@ def run_ours(args):
     search_avg_ms = search_ms / max(n_search, 1)
     achieved = bq * B / (search_avg_ms / 1e3) / 1e9
     peak, peak_kind = hbm_peak()
-    tr = profile_traffic(args, wp)
+    tr, tr_src = profile_traffic(args, wp)
+    prep_avg_ms = prep_ms / max(n_search, 1)
 
     # ---- end to end through the host API ----
     # every step's queries are staged in pinned host memory before timing; a
@@ -445,17 +517,18 @@ def run_ours(args):
     e2e = dist.world * B * args.steps / e2e_s
 
     # ---- recall and the CPU baseline (rank 0) ----
-    rec = cpu = None
+    rec = cpu = par = None
     if dist.rank == 0:
         from oracle import oracle as O
 
-        X = O.read_index(prefix) if not args.no_cpu_baseline else None
-        Xv = X.X if X is not None else ix.download()[2]
+        X = O.read_index(prefix)
+        Xv = X.X
         gtq = Qpool[:1000]
-        ix.search(gtq, k, L, args.search_mode)
         g_ids, _ = ix.search(gtq, k, L, args.search_mode)
         gt = ground_truth(Xv, gtq, k, device)
         rec = recall(g_ids, gt)
+        if args.parity_queries:
+            par = parity_check(ix, X, Qpool[:args.parity_queries], k, L, args.search_mode, device)
         if not args.no_cpu_baseline:
             cpu = cpu_baseline(X, np.concatenate([gtq, Qpool[1000:]]), L, k, args.cpu_seconds, gt_q=None)
             ids_cpu, _ = O.cpu_beam_search_batch(X.X, X.adj, X.medoid, gtq, L, k)
@@ -472,14 +545,18 @@ def run_ours(args):
                        "l2": f"index {index_device_bytes(info) / 1e9:.2f} GB larger than L2, not flushed; "
                              "fresh query batch every step"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": tr, "peak_source": f"{peak_kind} hbm_gbs",
-                         "kernel": "search_kernel", "kernel_ms": search_avg_ms,
-                         "bytes_per_query": bq, "per_query": {"H": H, "E": E, "C_r": Cr}},
+                         "frac": achieved / peak, "traffic": tr, "traffic_source": tr_src,
+                         "peak_source": f"{peak_kind} hbm_gbs", "kernel": "search_kernel",
+                         "kernel_ms": search_avg_ms, "prepare_ms": prep_avg_ms,
+                         "bytes_per_query": bq,
+                         "per_query": {"H": H, "E": E, "C_r": Cr, "E_p99": float(np.percentile(c[:, 1], 99)),
+                                       "E_max": int(c[:, 1].max())}},
             "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": B * wp["dim"] * 4,
                     "d2h_bytes_per_step": B * k * 8},
             "gpu_launches": (1 if args.search_mode == "exact_gpu" else 2) * args.steps,
             "clocks": clocks,
             "recall_at_10": rec,
+            "parity": par,
             "cpu_baseline": cpu,
         }
         emit(line)
@@ -732,6 +809,11 @@ def run_mixed(args):
 def main():
     args = parse_args()
     route_stdout_to_stderr()
+    if args.build_index_only:
+        single = Dist.__new__(Dist)
+        single.world, single.rank, single.local, single.pg = 1, 0, 0, None
+        ensure_index(args, workload_params(args.workload, args.n), 0, single)
+        return
     if args.impl == "reference":
         run_reference(args)
     elif args.mode == "insert":

@@ -39,6 +39,8 @@ dvs_status upload(Device& d, const HostIndex& h, uint32_t shard, uint32_t nshard
   DVS_CUDA(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
   DVS_CUDA(cudaEventCreate(&d.ev0));
   DVS_CUDA(cudaEventCreate(&d.ev1));
+  DVS_CUDA(cudaEventCreateWithFlags(&d.done, cudaEventDisableTiming));
+  DVS_CUDA(cudaEventRecord(d.done, d.stream));
   // records: reference layout -> [codes | pad to word | add | rescale | pad to 16 B]
   std::vector<uint32_t> rec(size_t(nl) * rec_words, 0u);
   std::vector<uint32_t> adj(size_t(nl) * R);
@@ -223,9 +225,21 @@ namespace dvs {
 dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L, dvs_mode mode,
                      uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st, bool timed,
                      bool out_slots) {
+  if (d.lay.R > 64) return fail(DVS_ERR_UNSUPPORTED, "max out-degree above 64 is not supported by the search kernel");
+  // after the previous search on this device, whichever stream it used
+  DVS_CUDA(cudaStreamWaitEvent(st, d.done, 0));
+  dvs_status rc = search_enqueue(ix, d, d_q, nq, k, L, mode, d_ids, d_dist, d_counters, st, timed, out_slots);
+  const cudaError_t e = cudaEventRecord(d.done, st);
+  if (rc == DVS_OK && e != cudaSuccess)
+    return fail(DVS_ERR_CUDA, std::string("cudaEventRecord: ") + cudaGetErrorString(e));
+  return rc;
+}
+
+dvs_status search_enqueue(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L,
+                          dvs_mode mode, uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st,
+                          bool timed, bool out_slots) {
   const DevLayout& lay = d.lay;
   const bool rabitq = mode == DVS_MODE_RABITQ_GPU;
-  if (lay.R > 64) return fail(DVS_ERR_UNSUPPORTED, "max out-degree above 64 is not supported by the search kernel");
   if (lay.n == 0) {
     // an index created empty and not yet inserted into: every result slot is empty
     if (timed) DVS_CUDA(cudaEventRecord(d.ev0, st));
@@ -247,17 +261,15 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
   const uint32_t blocks = std::max(1u, std::min(blocks_full, blocks_needed));
   const size_t slots = size_t(blocks) * s.wpb;
   if (slots > d.ovf_slots) {
+    // spill tables and their epoch words start zeroed: every entry empty
     dev_free(d.ovf);
-    DVS_CUDA(cudaMalloc(&d.ovf, slots * kOverflowSlots * 4));
+    DVS_CUDA(cudaMalloc(&d.ovf, slots * (size_t(kOverflowSlots) + 1) * 4));
+    DVS_CUDA(cudaMemsetAsync(d.ovf, 0, slots * (size_t(kOverflowSlots) + 1) * 4, st));
     d.ovf_slots = slots;
   }
   DVS_CUDA(cudaMemsetAsync(d.work, 0, 16, st));
   cudaEvent_t* tr = nullptr;
-  if (ix->kernel_timing) {
-    if (d.tev.empty()) {
-      d.tev.resize(3 * Device::kRing);
-      for (auto& e : d.tev) DVS_CUDA(cudaEventCreate(&e));
-    }
+  if (ix->kernel_timing && !d.tev.empty()) {
     if (d.tcount < Device::kRing) tr = &d.tev[3 * d.tcount++];
   }
   if (timed) DVS_CUDA(cudaEventRecord(d.ev0, st));
@@ -287,8 +299,10 @@ dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, ui
   a.counters = d_counters ? d_counters : d.counters;
   a.work = d.work;
   a.ovf = d.ovf;
+  a.ovf_epoch = d.ovf + d.ovf_slots * kOverflowSlots;
   a.ovf_cap = kOverflowSlots;
   a.ovf_limit = kOverflowSlots / 10 * 8;
+  a.ovf_tagged = lay.n < (uint64_t(1) << 24) ? 1u : 0u;
   a.hcap = s.hcap;
   a.hlimit = s.hlimit;
   a.vt16 = s.vt16;
@@ -485,6 +499,16 @@ dvs_status dvs_set_rotation(dvs_index* ix, dvs_rotation rotation) {
 dvs_status dvs_set_kernel_timing(dvs_index* ix, int enable) {
   if (!ix) return fail(DVS_ERR_ARG, "null index");
   std::lock_guard<std::mutex> g(ix->mu);
+  if (enable) {
+    // the event ring is made here, not by the first timed search, so that
+    // creating its events never stalls a timed loop
+    for (auto& d : ix->devs) {
+      if (!d.tev.empty()) continue;
+      DVS_CUDA(cudaSetDevice(d.ordinal));
+      d.tev.resize(3 * dvs::Device::kRing);
+      for (auto& e : d.tev) DVS_CUDA(cudaEventCreate(&e));
+    }
+  }
   ix->kernel_timing = enable != 0;
   return DVS_OK;
 }
@@ -686,39 +710,3 @@ dvs_status dvs_l2_distances(const float* d_query, const float* d_candidates, flo
 }
 
 }  // extern "C"
-
-// ---------------------------------------------------------------------------
-// Read-only views for entry points defined in other translation units.
-// ---------------------------------------------------------------------------
-namespace dvs {
-
-dvs_status device_view(dvs_index* ix, uint32_t slot, DeviceView* out) {
-  if (!ix || !out) return fail(DVS_ERR_ARG, "null argument");
-  if (slot >= ix->devs.size()) return fail(DVS_ERR_ARG, "device slot out of range");
-  const Device& d = ix->devs[slot];
-  out->lay = d.lay;
-  out->ordinal = d.ordinal;
-  out->sm_count = d.sm_count;
-  out->stream = d.stream;
-  out->hop_limit = ix->hop_limit;
-  out->index_dim = ix->host.info.dim;
-  return DVS_OK;
-}
-
-dvs_status search_shape(dvs_index* ix, uint32_t slot, uint32_t cap, bool exact, SearchShape* out) {
-  if (!ix || !out || slot >= ix->devs.size()) return fail(DVS_ERR_ARG, "bad argument");
-  LaunchShape s;
-  const dvs_status rc = launch_shape(ix->devs[slot], cap, ix->slots_per_entry, exact, s);
-  if (rc != DVS_OK) return rc;
-  out->cap = s.cap;
-  out->cap_pad = s.cap_pad;
-  out->hcap = s.hcap;
-  out->hlimit = s.hlimit;
-  out->vt16 = s.vt16;
-  out->hbuckets = s.hbuckets;
-  out->wpb = s.wpb;
-  out->blocks_per_sm = s.blocks_per_sm;
-  return DVS_OK;
-}
-
-}  // namespace dvs

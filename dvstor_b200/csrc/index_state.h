@@ -51,6 +51,10 @@ struct Device {
   int ordinal = 0;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  // recorded after every search's work on whatever stream it ran; the next
+  // search on this device waits for it, so calls on different streams never
+  // overlap on the library's scratch
+  cudaEvent_t done = nullptr;
   uint32_t sm_count = 0;
   uint32_t shard = 0;     // shard held (sharded placement), rows = its row count
   uint64_t rows = 0;
@@ -117,6 +121,8 @@ struct Device {
     for (auto& e : ins_ev) e = nullptr;
     if (ev0) cudaEventDestroy(ev0);
     if (ev1) cudaEventDestroy(ev1);
+    if (done) cudaEventDestroy(done);
+    done = nullptr;
     for (cudaEvent_t e : tev) cudaEventDestroy(e);
     tev.clear();
     if (stream) cudaStreamDestroy(stream);
@@ -133,6 +139,11 @@ dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path);
 dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L, dvs_mode mode,
                      uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st, bool timed,
                      bool out_slots = false);
+
+// search_on's work without the ordering against other searches on the device.
+dvs_status search_enqueue(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L,
+                          dvs_mode mode, uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st,
+                          bool timed, bool out_slots);
 
 // Grows the device arrays of a replicated index to hold `rows` nodes (online insert).
 dvs_status grow_rows(Device& d, uint64_t rows);

@@ -34,31 +34,46 @@ namespace {
 
 constexpr uint32_t kFull = 0xFFFFFFFFu;
 
-// Inserts `id` into a linear-probing table; true when it was not present.
-// The table never fills: callers keep its load under the limit.
-__device__ __forceinline__ bool table_insert(uint32_t* tab, uint32_t cap, uint32_t id) {
+// Per-warp spill table in global memory (linear probing).  For indexes of
+// fewer than 2^24 nodes an entry is (epoch << 24) | id, and an entry whose
+// epoch is not the query's own counts as empty: a query takes a fresh epoch
+// instead of clearing the table, which is cleared only when the 8-bit epoch
+// wraps.  Larger indexes store the bare id with kEmptySlot as empty, and the
+// table is cleared by the query that first spills.  `tag` is the query's
+// epoch << 24 (0 for the bare form).  Slots never become empty during a query,
+// so a probe chain ends at the first empty slot.
+__device__ __forceinline__ bool spill_empty(uint32_t v, uint32_t tag) {
+  return tag ? (v & 0xFF000000u) != tag : v == kEmptySlot;
+}
+
+// Inserts `id`; true when it was not present.  The table never fills: callers
+// keep its load under the limit.
+__device__ __forceinline__ bool table_insert(uint32_t* tab, uint32_t cap, uint32_t id, uint32_t tag) {
   volatile uint32_t* vt = tab;
+  const uint32_t key = tag | id;
   uint32_t s = hash_slot(id, cap);
   for (uint32_t probe = 0; probe < cap; ++probe) {
-    const uint32_t cur = vt[s];
-    if (cur == id) return false;
-    if (cur == kEmptySlot) {
-      const uint32_t old = atomicCAS(tab + s, kEmptySlot, id);
-      if (old == kEmptySlot) return true;
-      if (old == id) return false;
+    uint32_t cur = vt[s];
+    for (int tries = 0; tries < 32; ++tries) {  // another lane of the warp may take the slot first
+      if (cur == key) return false;
+      if (!spill_empty(cur, tag)) break;
+      const uint32_t old = atomicCAS(tab + s, cur, key);
+      if (old == cur) return true;
+      cur = old;
     }
     s = (s + 1 == cap) ? 0 : s + 1;
   }
   return false;
 }
 
-__device__ __forceinline__ bool table_contains(const uint32_t* tab, uint32_t cap, uint32_t id) {
+__device__ __forceinline__ bool table_contains(const uint32_t* tab, uint32_t cap, uint32_t id, uint32_t tag) {
   const volatile uint32_t* vt = tab;
+  const uint32_t key = tag | id;
   uint32_t s = hash_slot(id, cap);
   for (uint32_t probe = 0; probe < cap; ++probe) {
     const uint32_t cur = vt[s];
-    if (cur == id) return true;
-    if (cur == kEmptySlot) return false;
+    if (cur == key) return true;
+    if (spill_empty(cur, tag)) return false;
     s = (s + 1 == cap) ? 0 : s + 1;
   }
   return false;
@@ -457,6 +472,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       err = kErrNonFinite;
     }
     bool overflow = false;
+    uint32_t gtag = 0;
     uint32_t pf_node = kEmptySlot, pf[NPL];
 
     for (;;) {
@@ -528,7 +544,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
         const bool may_insert = hcount + 32 <= a.hlimit;
         bool full = false;
         if (first) {
-          const bool in_spill = overflow && table_contains(gtab, a.ovf_cap, id);
+          const bool in_spill = overflow && table_contains(gtab, a.ovf_cap, id, gtag);
           if (!in_spill) {
             uint32_t r;
             if (a.vt16) {
@@ -548,9 +564,22 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
               err |= kErrCapacity;
               break;
             }
-            uint4* g4 = reinterpret_cast<uint4*>(gtab);
-            const uint4 e = make_uint4(kEmptySlot, kEmptySlot, kEmptySlot, kEmptySlot);
-            for (uint32_t j = lane; j < (a.ovf_cap >> 2); j += 32) g4[j] = e;
+            // a fresh epoch for this query's entries; the table is cleared only
+            // when the epoch wraps (or, for bare ids, every time)
+            uint32_t ep = 0;
+            if (lane == 0) ep = a.ovf_epoch[warp_slot];
+            ep = __shfl_sync(kFull, ep, 0) + 1;
+            const bool clear = !a.ovf_tagged || ep > 255u;
+            if (clear) {
+              uint4* g4 = reinterpret_cast<uint4*>(gtab);
+              const uint32_t f = a.ovf_tagged ? 0u : kEmptySlot;
+              const uint4 e = make_uint4(f, f, f, f);
+              for (uint32_t j = lane; j < (a.ovf_cap >> 2); j += 32) g4[j] = e;
+              if (ep > 255u) ep = 1;
+            }
+            // bare ids leave the next tagged query a wrapped epoch, so it clears
+            if (lane == 0) a.ovf_epoch[warp_slot] = a.ovf_tagged ? ep : 255u;
+            gtag = a.ovf_tagged ? ep << 24 : 0u;
             __syncwarp();
             overflow = true;
           }
@@ -558,7 +587,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
             err |= kErrCapacity;
             break;
           }
-          if (full) fresh[s] = table_insert(gtab, a.ovf_cap, id);
+          if (full) fresh[s] = table_insert(gtab, a.ovf_cap, id, gtag);
           gcount += __popc(__ballot_sync(kFull, full && fresh[s]));
         }
         const uint32_t cnt = __popc(__ballot_sync(kFull, fresh[s]));

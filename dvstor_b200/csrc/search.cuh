@@ -59,29 +59,16 @@ struct SearchArgs {
   float* out_dist = nullptr;
   uint32_t* counters = nullptr;     // nq*4: H, E, C_r, count | error bits << 16
   uint32_t* work = nullptr;         // [0] next query, [1] error bits, [2] overflowed queries
-  uint32_t* ovf = nullptr;          // per warp slot visited overflow tables
+  uint32_t* ovf = nullptr;          // per warp slot visited spill tables (ovf_cap words each), zeroed at allocation
+  uint32_t* ovf_epoch = nullptr;    // per warp slot epoch of its table (zeroed at allocation)
   uint32_t ovf_cap = 0, ovf_limit = 0;
+  uint32_t ovf_tagged = 0;          // 1: entries are (epoch << 24) | id (indexes of fewer than 2^24 nodes)
   uint32_t hcap = 0, hlimit = 0;    // shared-memory visited table: words, entry limit
   uint32_t vt16 = 0;                // compact 16-bit two-choice table: its hash width (20 or 24), 0 = 32-bit table
   uint32_t hbuckets = 0;            // its bucket count (8 entries each)
   float inv_hbuckets = 0.f;
   uint32_t cap_pad = 0, dim_pad = 0;
   uint32_t out_slots = 0;           // 1: results are dense slots (online insert), else stored node ids
-};
-
-// What another translation unit may read of an open index's device copy.
-struct DeviceView {
-  DevLayout lay;
-  int ordinal = 0;
-  uint32_t sm_count = 0;
-  cudaStream_t stream = nullptr;
-  uint32_t hop_limit = 0;
-  uint32_t index_dim = 0;
-};
-
-// Launch shape of the search kernel for one beam capacity.
-struct SearchShape {
-  uint32_t cap = 0, cap_pad = 0, hcap = 0, hlimit = 0, vt16 = 0, hbuckets = 0, wpb = 0, blocks_per_sm = 0;
 };
 
 constexpr int kMaxBlockSmem = 227 * 1024;  // dynamic shared memory a block may have on sm_100
@@ -159,8 +146,6 @@ bool search_wide_records(bool exact, uint32_t code_words);
 
 struct dvs_index;
 namespace dvs {
-dvs_status device_view(dvs_index* ix, uint32_t slot, DeviceView* out);
-dvs_status search_shape(dvs_index* ix, uint32_t slot, uint32_t cap, bool exact, SearchShape* out);
 
 cudaError_t launch_estimate_ref_layout(const float* qrot, const float* f3, const uint8_t* records, float* out,
                                        uint32_t n, uint32_t dim, uint32_t bits, cudaStream_t stream);

@@ -135,7 +135,10 @@ dvs_status dvs_search(dvs_index* index, const float* h_queries, uint32_t nq, uin
  * rows C_r, and result count | error bits << 16 (1: visited set over capacity,
  * 2: expansion limit, 8: the query held a NaN or an infinity and was not
  * searched — its result slots are empty).  dvs_search reports the same
- * conditions as DVS_ERR_CAPACITY, DVS_ERR_HOP_LIMIT and DVS_ERR_ARG. */
+ * conditions as DVS_ERR_CAPACITY, DVS_ERR_HOP_LIMIT and DVS_ERR_ARG.  A NULL
+ * stream means the index's internal stream.  Searches on one device run on
+ * the GPU one after another, whichever streams they are given (they share the
+ * index's scratch). */
 dvs_status dvs_search_device(dvs_index* index, uint32_t device_slot, const float* d_queries, uint32_t nq,
                              uint32_t dim, uint32_t k, uint32_t beam_width, dvs_mode mode, uint32_t* d_out_ids,
                              float* d_out_dist, uint32_t* d_counters, void* stream);
@@ -145,12 +148,16 @@ dvs_status dvs_search_device(dvs_index* index, uint32_t device_slot, const float
  * free memory for its own pool, a request path where allocation is
  * forbidden).  No counterpart in the reference.  Same arguments and results
  * as dvs_search_device; the scratch (rotated queries, factors, work counters,
- * visited-set spill tables) comes from one fixed 16 MiB __device__ array per
- * GPU instead of cudaMalloc, which caps a call at
- * 8 MiB / (4*round_up(dim,4) + 16) queries (20,971 at dim 96; more returns
- * DVS_ERR_CAPACITY).  The first call on a device looks the array up with
- * cudaGetSymbolAddress; make it before any stream capture.  Calls share the
- * array: calls whose work overlaps on the GPU race and must be serialised. */
+ * visited-set spill tables of the same size as dvs_search_device's) comes from
+ * one fixed 64 MiB __device__ array per GPU instead of cudaMalloc.  That caps
+ * a call at (8 MiB - 256) / (4*round_up(dim,4) + 16) queries (20,970 at dim 96;
+ * more returns DVS_ERR_CAPACITY) and at 895 warps in flight, so a call runs
+ * slower than dvs_search_device on a full GPU.  The first call on a device
+ * looks the array up with cudaGetSymbolAddress; make it before any stream
+ * capture.  A NULL stream means the index's internal stream.  Calls on one
+ * index and device are ordered on the GPU after that index's other searches;
+ * calls on different indexes whose work overlaps on the GPU race on the shared
+ * array and must be serialised by the caller. */
 dvs_status dvs_search_device_noalloc(dvs_index* index, uint32_t device_slot, const float* d_queries, uint32_t nq,
                                      uint32_t dim, uint32_t k, uint32_t beam_width, dvs_mode mode,
                                      uint32_t* d_out_ids, float* d_out_dist, uint32_t* d_counters, void* stream);

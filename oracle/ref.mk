@@ -3,7 +3,8 @@
 # launcher and its kernel header are needed (src/gpu/gpu_kernel_launcher.cu,
 # src/gpu/kernels/distance_kernels.cuh; CUDA runtime + cuBLAS); the rest of the
 # reference needs Eigen, Boost, oneTBB and ibverbs and is not built.
-REF ?= /root/reference
+# REF: the reference project's root (DVS_REFERENCE_ROOT, else where the build environment mounts it)
+REF ?= $(or $(DVS_REFERENCE_ROOT),/root/reference)
 HERE := $(dir $(abspath $(lastword $(MAKEFILE_LIST))))
 NVCC ?= /usr/local/cuda/bin/nvcc
 OUT := $(HERE)_ref/libref_gpu.so

@@ -46,15 +46,22 @@ def test_bytes_per_query_formula():
         4 * D + H * (4 * R + 1) + E * 4 * D + 8 * k)
 
 
-def test_profile_traffic_only_for_the_profiled_workload():
+def test_profile_traffic_only_for_the_profiled_workload_and_sources():
     a = _args()
     wp = bench.workload_params(a.workload, a.n)
-    tr = bench.profile_traffic(a, wp)
-    assert tr is not None and tr > 1e9
+    tr, src = bench.profile_traffic(a, wp)
+    digest = None
+    for ln in open(bench.PROFILE_SUMMARY):
+        if ln.startswith("kernel_sources_sha256_16="):
+            digest = ln.split("=", 1)[1].split()[0]
+    if digest == bench.kernel_sources_digest():
+        assert tr is not None and tr > 1e9
+    else:  # a capture of older kernel sources is not reported as this kernel's traffic
+        assert tr is None and "does not match" in src
     for argv in (["--workload", "lowrank-1m-d960"], ["--search-mode", "exact_gpu"], ["--bits", "8"],
                  ["--k", "100"], ["--batch", "1000"], ["--n", "200000"]):
         b = _args(*argv)
-        assert bench.profile_traffic(b, bench.workload_params(b.workload, b.n)) is None
+        assert bench.profile_traffic(b, bench.workload_params(b.workload, b.n))[0] is None
 
 
 def test_index_cache_tag_follows_the_bit_width():

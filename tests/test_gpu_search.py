@@ -159,6 +159,31 @@ def test_overflow_path_is_exact(gpu, oracle, cases):
     assert st["estimates"] == int(o_cnt[:, 1].sum())
 
 
+def test_spill_table_epochs_wrap(gpu, oracle, cases):
+    """A warp's spill table is not cleared between queries: each spilling query
+    takes the next 8-bit epoch, and entries of other epochs count as empty.
+    300 back-to-back searches give every warp slot more spilling queries than
+    there are epochs, so the table is reused under every epoch and cleared at
+    the wrap; every search must still equal the oracle."""
+    import torch
+
+    case = cases["gauss96"]
+    Q = normalized_gaussian(64, 96, 22)
+    o_ids, o_d, o_cnt, b_ids, b_d = case.idx.knn(Q, 10, 64, beam_cap=128)
+    with gpu.Index(case.prefix) as ix:
+        ix.set_visited_slots(2)
+        dq = torch.from_numpy(Q).cuda()
+        c = torch.zeros((64, 4), dtype=torch.int32, device="cuda")
+        outs = []
+        for _ in range(300):
+            ids, d = ix.search_device(dq, 10, 64, d_counters=c)
+            outs.append((ids.clone(), d.clone(), c.clone()))
+        torch.cuda.synchronize()
+    for ids, d, cnt in outs:
+        assert_results_match(ids.cpu().numpy().view(np.uint32), d.cpu().numpy(), o_ids, o_d, b_ids, b_d)
+        np.testing.assert_array_equal(cnt.cpu().numpy().view(np.uint32)[:, :3], o_cnt[:, :3])
+
+
 def test_hop_limit_reports_error(gpu, cases):
     case = cases["gauss96"]
     with gpu.Index(case.prefix) as ix:
