@@ -72,6 +72,14 @@ def parse_args():
     ap.add_argument("--alpha", type=float, default=1.2)
     ap.add_argument("--placement", choices=["replicate", "shard"], default="replicate",
                     help="shard: one process over --gpus devices, the index split by slot (run without torchrun)")
+    ap.add_argument("--metric", choices=["l2", "ip"], default=None,
+                    help="index metric (default: ip for --mode mixed, else l2)")
+    ap.add_argument("--clients", type=int, default=16, help="--mode mixed: client threads per GPU")
+    ap.add_argument("--read-ratio", type=float, default=0.5, help="--mode mixed: fraction of operations that are queries")
+    ap.add_argument("--seconds", type=float, default=20.0, help="--mode mixed: measured seconds")
+    ap.add_argument("--warmup-seconds", type=float, default=5.0, help="--mode mixed: warm-up seconds")
+    ap.add_argument("--reserve", type=int, default=400_000, help="--mode mixed: insert capacity reserved up front")
+    ap.add_argument("--report", default=None, help="--mode mixed: path of the breakdown JSON report")
     ap.add_argument("--parity-queries", type=int, default=500,
                     help="queries of the workload checked against the oracle's Vamana::knn after the timed region")
     ap.add_argument("--build-index-only", action="store_true", help=argparse.SUPPRESS)
@@ -143,8 +151,14 @@ def workload_params(name, n=None):
     return dict(gen=gen, n=n or n0, dim=dim, seed=seed, R=R, build_L=build_L, search_L=search_L, k=k)
 
 
+def index_metric(args) -> str:
+    return args.metric or ("ip" if args.mode == "mixed" else "l2")
+
+
 def index_prefix(args, wp):
     tag = f"{args.workload}_n{wp['n']}_R{wp['R']}_L{wp['build_L']}_b{args.bits}_s1234"
+    if index_metric(args) != "l2":
+        tag += f"_{index_metric(args)}"
     return os.path.join(args.cache, tag, "idx")
 
 
@@ -156,7 +170,7 @@ def ensure_index(args, wp, device, dist, subprocess_build=False):
     done = prefix + ".done"
     if dist.local == 0 and not os.path.exists(done) and subprocess_build:
         cmd = [sys.executable, os.path.abspath(__file__), "--build-index-only", "--workload", args.workload,
-               "--bits", str(args.bits), "--cache", args.cache]
+               "--bits", str(args.bits), "--cache", args.cache, "--metric", index_metric(args)]
         if args.n:
             cmd += ["--n", str(args.n)]
         subprocess.run(cmd, check=True, stdout=sys.stderr)
@@ -168,7 +182,7 @@ def ensure_index(args, wp, device, dist, subprocess_build=False):
         log(f"[bench] generated {X.shape} in {time.time() - t:.1f}s; building index on cuda:{device}")
         t = time.time()
         st = build_index(X, prefix, R=wp["R"], beam_width=wp["build_L"], alpha=1.2, rabitq_bits=args.bits,
-                         seed=1234, device=device)
+                         seed=1234, device=device, metric=index_metric(args))
         log(f"[bench] built in {time.time() - t:.1f}s ({st})")
         open(done, "w").write(json.dumps(st))
     dist.barrier()
@@ -742,68 +756,141 @@ def run_insert(args):
 
 
 def run_mixed(args):
-    """Queries and inserts interleaved (the 50/50 query/insert serving mix): each
-    step searches --batch device-resident queries (k, beam width) and inserts
-    --insert-batch host vectors through dvs_insert (beam width construction,
-    alpha); wall clock around the pair, synchronised.  Operations/s counts both."""
+    """The dynamic serving mix (Vamana::knn and Vamana::insert served
+    concurrently): --clients client threads per GPU, each issuing one operation
+    at a time and waiting for it, a query (k, beam width) with probability
+    --read-ratio and otherwise a single-vector insert (beam width
+    construction, alpha), for --seconds after --warmup-seconds; the
+    inner-product metric by default.  Operations go through
+    dvstor_b200.serving.BatchingServer (pending queries batched into one
+    dvs_search call, pending inserts into one dvs_insert call).  Reports
+    operations/s, queries/s, inserts/s and p50/p95/p99 latency per operation,
+    and writes the reference's breakdown JSON report (--report).  Under
+    torchrun every rank serves its own replica with its own clients and
+    inserts (weak scaling); time = max over ranks."""
     import torch
 
     import dvstor_b200 as D
     from dvstor_b200 import datasets
+    from dvstor_b200.serving import BatchingServer, Breakdown
 
-    dist = Dist("gloo")
+    dist = Dist("nccl" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "gloo")
+    device = dist.local
+    torch.cuda.set_device(device)
     wp = workload_params(args.workload, args.n)
     L = args.beam_width or wp["search_L"]
-    k, Bq, Bi = args.k, args.batch, args.insert_batch
-    prefix = ensure_index(args, wp, 0, dist)
-    torch.cuda.set_device(0)
-    ix = D.Index(prefix, devices=(0,))
+    k = args.k
+    prefix = ensure_index(args, wp, device, dist)
+    ix = D.Index(prefix, devices=(device,))
     n0 = int(ix.info.num_vectors)
-    nsteps = args.warmup + args.steps
-    Q = torch.from_numpy(datasets.queries_for(args.workload, Bq * nsteps, stream=3)).cuda().view(nsteps, Bq, -1)
-    Xn = datasets.queries_for(args.workload, Bi * nsteps, stream=9)
-    ids = np.arange(n0, n0 + Bi * nsteps, dtype=np.uint32)
-    ix.reserve(n0 + Bi * nsteps)
-    out_i = torch.empty((Bq, k), dtype=torch.int32, device="cuda")
-    out_d = torch.empty((Bq, k), dtype=torch.float32, device="cuda")
-    stream = torch.cuda.Stream()
+    ix.reserve(n0 + args.reserve)
+    bd = Breakdown()
+    server = BatchingServer(ix, k, L, args.search_mode, args.beam_width_construction, args.alpha, breakdown=bd)
+    Qpool = datasets.queries_for(args.workload, 65536, stream=3 + 100 * dist.rank)
+    Xpool = datasets.queries_for(args.workload, 65536, stream=9 + 100 * dist.rank)
+    id_lock = threading.Lock()
+    next_id = [n0]
+    inserted = []
+    phase = {"measure": False, "stop": False}
+    counts = {"query": 0, "insert": 0}
 
-    def step(s):
-        ix.search_device(Q[s], k, L, d_out_ids=out_i, d_out_dist=out_d, stream=stream)
-        stream.synchronize()
-        ix.insert(Xn[s * Bi:(s + 1) * Bi], ids[s * Bi:(s + 1) * Bi], beam_width_construction=args.beam_width_construction,
-                  alpha=args.alpha, max_batch=Bi)
+    def client(c):
+        rng = np.random.default_rng([5, dist.rank, c])
+        i = c
+        while not phase["stop"]:
+            if rng.random() < args.read_ratio:
+                server.search(Qpool[i % len(Qpool)])
+                kind = "query"
+            else:
+                with id_lock:
+                    ident = next_id[0]
+                    next_id[0] += 1
+                server.insert(ident, Xpool[(ident - n0) % len(Xpool)])
+                inserted.append(ident)
+                kind = "insert"
+            if phase["measure"]:
+                counts[kind] += 1
+            i += args.clients
 
-    for s in range(args.warmup):
-        step(s)
-    torch.cuda.synchronize()
-    sampler = clocks_sampler(0)
+    threads = [threading.Thread(target=client, args=(c,), daemon=True) for c in range(args.clients)]
+    dist.barrier()
+    for t in threads:
+        t.start()
+    time.sleep(args.warmup_seconds)
+    bd.__init__()  # the report covers the measured window only
+    batches0 = dict(server.batches)
+    sampler = clocks_sampler(device)
     t_wall0 = time.time()
-    t = time.perf_counter()
-    for s in range(args.warmup, nsteps):
-        step(s)
-    torch.cuda.synchronize()
-    el = time.perf_counter() - t
-    clocks = clocks_summary(sampler, t_wall0, time.time())
-    probe = slice(Bi * args.warmup, Bi * args.warmup + 1000)
-    got, _ = ix.search(Xn[probe], 10, 64)
-    self_hit = float((got[:, 0] == ids[probe]).mean())
+    t0 = time.perf_counter()
+    phase["measure"] = True
+    time.sleep(args.seconds)
+    phase["measure"] = False
+    el = time.perf_counter() - t0
+    t_wall1 = time.time()
+    phase["stop"] = True
+    for t in threads:
+        t.join()
+    server.close()
+    clocks = clocks_summary(sampler, t_wall0, t_wall1)
+    batches = {kk: server.batches[kk] - batches0[kk] for kk in batches0}
+    rep = bd.report(meta={"client_threads": args.clients, "read_ratio": args.read_ratio, "dim": wp["dim"],
+                          "search_mode": args.search_mode, "measure_seconds": args.seconds,
+                          "warmup_seconds": args.warmup_seconds, "operation_granularity": "single_vector",
+                          "workload": "mixed", "batching": "pending queries per dvs_search, pending inserts "
+                                                           "per dvs_insert", "rank": dist.rank})
+    # the inserted vectors are found again (rank 0 = themselves)
+    probe = np.array(inserted[:1000], np.int64)
+    self_hit = None
+    if len(probe):
+        got, _ = ix.search(Xpool[(probe - n0) % len(Xpool)], 10, L, args.search_mode)
+        self_hit = float((got[:, 0] == probe.astype(np.uint32)).mean())
     ix.close()
-    ops = (Bq + Bi) * args.steps
-    line = {
-        "metric": f"operations/sec, 50/50 queries (k={k}, L={L}) and inserts (L_c={args.beam_width_construction})",
-        "value": ops / el, "unit": "ops/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "n_base": n0, "dim": wp["dim"], "R": wp["R"], "rabitq_bits": args.bits,
-                   "queries_per_step": Bq, "inserts_per_step": Bi, "metric": "l2 (normalised vectors: the same "
-                   "ranking as ip; estimates and rerank are L2 in both reference modes)"},
-        "queries_per_s": Bq * args.steps / el, "inserts_per_s": Bi * args.steps / el,
-        "e2e": {"value": ops / el, "unit": "ops/s", "h2d_bytes_per_step": Bi * (wp["dim"] * 4 + 4),
-                "d2h_bytes_per_step": 0},
-        "self_hit_at_1": self_hit, "clocks": clocks,
-    }
-    emit(line)
+    el_max = dist.max(el)
+    tot_q = counts["query"]
+    if dist.world > 1:
+        import torch.distributed as tdist
+
+        t = torch.tensor([counts["query"], counts["insert"]], dtype=torch.float64, device=f"cuda:{device}")
+        tdist.all_reduce(t)
+        tot_q, tot_i = float(t[0]), float(t[1])
+    else:
+        tot_i = counts["insert"]
+    if args.report:
+        path = args.report if dist.world == 1 else f"{args.report}.rank{dist.rank}"
+        os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+        open(path, "w").write(json.dumps(rep, indent=2, sort_keys=True))
+
+    def lat(op):
+        j = rep.get(f"{op}_breakdown")
+        if not j:
+            return None
+        l_ = j["latency"]
+        return {"count": j["count"], "mean_ms": l_["mean_end_to_end_ns"] / 1e6, "p50_ms": l_["p50_end_to_end_ns"] / 1e6,
+                "p95_ms": l_["p95_end_to_end_ns"] / 1e6, "p99_ms": l_["p99_end_to_end_ns"] / 1e6,
+                "mean_queue_wait_ms": l_["mean_queue_wait_ns"] / 1e6, "gpu_share": (
+                    j["breakdown"]["gpu_ns"] / l_["service_ns"] if l_["service_ns"] else None)}
+
+    if dist.rank == 0:
+        ops = (tot_q + tot_i) / el_max
+        line = {
+            "metric": f"operations/sec, {args.clients} client streams per GPU, {int(args.read_ratio * 100)}% queries "
+                      f"(k={k}, L={L}) / single-vector inserts (L_c={args.beam_width_construction})",
+            "value": ops, "unit": "ops/s", "n_gpus": dist.world, "steps": args.seconds, "warmup": args.warmup_seconds,
+            "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "n_base": n0, "dim": wp["dim"], "R": wp["R"],
+                       "rabitq_bits": args.bits, "metric": args.metric or "ip", "clients_per_gpu": args.clients,
+                       "read_ratio": args.read_ratio, "measure_seconds": args.seconds,
+                       "parallelism": f"replicas x{dist.world}, each with its own clients and inserts"},
+            "queries_per_s": tot_q / el_max, "inserts_per_s": tot_i / el_max,
+            "latency": {"query": lat("query"), "insert": lat("insert")},
+            "batches": batches, "self_hit_at_1": self_hit,
+            "e2e": {"value": ops, "unit": "ops/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None},
+            "clocks": clocks, "report": args.report,
+        }
+        emit(line)
+    dist.barrier()
+    dist.close()
 
 
 def main():

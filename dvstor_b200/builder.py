@@ -24,10 +24,12 @@ class BuildStats(C.Structure):
 
 def build_index(X, prefix: str | None, R: int = 32, beam_width: int = 128, alpha: float = 1.2, rabitq_bits: int = 4,
                 seed: int = 1234, num_memory_nodes: int = 1, device: int = 0, batch_cap: int = 0,
-                visited_cap: int = 0, return_arrays: bool = False):
+                visited_cap: int = 0, return_arrays: bool = False, metric: str = "l2"):
     """Builds an index from X (n, dim) float32 on `device`; writes the offline
     files at `prefix` when given.  Returns a stats dict (plus adj and records
-    when return_arrays)."""
+    when return_arrays).  metric "ip" marks the index inner-product (the
+    search seeds with 1 - dot); the graph is built with L2 distances, which on
+    unit-norm vectors rank exactly as inner product does."""
     X = np.ascontiguousarray(X, dtype=np.float32)
     n, d = X.shape
     adj = np.empty((n, R), np.uint32) if return_arrays else None
@@ -35,7 +37,7 @@ def build_index(X, prefix: str | None, R: int = 32, beam_width: int = 128, alpha
     if prefix:
         os.makedirs(os.path.dirname(os.path.abspath(prefix)), exist_ok=True)
     p = BuildParams(prefix.encode() if prefix else None, R, beam_width, alpha, rabitq_bits, seed, num_memory_nodes,
-                    _lib.METRIC["l2"], device, batch_cap, visited_cap, ptr(adj), ptr(rec))
+                    _lib.METRIC[metric], device, batch_cap, visited_cap, ptr(adj), ptr(rec))
     st = BuildStats()
     L = lib()
     fn = L.dvs_build_index

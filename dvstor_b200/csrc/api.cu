@@ -276,7 +276,7 @@ dvs_status search_enqueue(dvs_index* ix, Device& d, const float* d_q, uint32_t n
   if (tr) DVS_CUDA(cudaEventRecord(tr[0], st));
   if (rabitq) {
     if (ix->rotation == DVS_ROTATION_TENSOR)
-      DVS_CUDA(launch_prepare_tc(d_q, lay.dim, lay.P, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits,
+      DVS_CUDA(launch_prepare_tc(d_q, lay.dim, d.tc, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits,
                                  nq, d.work + 1, st));
     else
       DVS_CUDA(launch_prepare(d_q, lay.dim, lay.P, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits, nq,
@@ -307,7 +307,7 @@ dvs_status search_enqueue(dvs_index* ix, Device& d, const float* d_q, uint32_t n
   a.hlimit = s.hlimit;
   a.vt16 = s.vt16;
   a.hbuckets = s.hbuckets;
-  a.inv_hbuckets = s.hbuckets ? 1.0f / float(s.hbuckets) : 0.f;
+  a.hb_magic = s.hbuckets ? uint32_t(0xFFFFFFFFull / s.hbuckets + 1) : 0u;
   a.cap_pad = s.cap_pad;
   a.dim_pad = lay.vec_stride;
   a.out_slots = out_slots ? 1u : 0u;
@@ -492,6 +492,16 @@ dvs_status dvs_set_rotation(dvs_index* ix, dvs_rotation rotation) {
   if (!ix) return fail(DVS_ERR_ARG, "null index");
   if (rotation != DVS_ROTATION_EXACT && rotation != DVS_ROTATION_TENSOR) return fail(DVS_ERR_ARG, "unknown rotation");
   std::lock_guard<std::mutex> g(ix->mu);
+  if (rotation == DVS_ROTATION_TENSOR) {
+    // P split into tf32 planes once per device, read by every tensor-core rotation
+    for (auto& d : ix->devs) {
+      if (d.tc.split) continue;
+      DVS_CUDA(cudaSetDevice(d.ordinal));
+      DVS_CUDA(cudaStreamSynchronize(d.stream));
+      DVS_CUDA(dvs::tc_rotation_prepare(d.P, d.lay.dim, &d.tc, d.stream));
+      DVS_CUDA(cudaStreamSynchronize(d.stream));
+    }
+  }
   ix->rotation = rotation;
   return DVS_OK;
 }
@@ -681,7 +691,13 @@ dvs_status dvs_query_prepare_tc(const float* d_query, const float* d_P, const fl
   uint32_t* d_err = nullptr;
   DVS_CUDA(cudaMallocAsync(&d_err, 4, st));
   DVS_CUDA(cudaMemsetAsync(d_err, 0, 4, st));
-  DVS_CUDA(dvs::launch_prepare_tc(d_query, dim, d_P, d_centroid, d_rot_query, dim, d_factor, 3, dim, bits, nq, d_err,
+  // P is split for this call alone (an open index keeps its split)
+  struct Split {
+    dvs::TcRotation t;
+    ~Split() { dvs::tc_rotation_release(&t); }
+  } sp;
+  DVS_CUDA(dvs::tc_rotation_prepare(d_P, dim, &sp.t, st));
+  DVS_CUDA(dvs::launch_prepare_tc(d_query, dim, sp.t, d_centroid, d_rot_query, dim, d_factor, 3, dim, bits, nq, d_err,
                                   st));
   uint32_t h_err = 0;
   DVS_CUDA(cudaMemcpyAsync(&h_err, d_err, 4, cudaMemcpyDeviceToHost, st));

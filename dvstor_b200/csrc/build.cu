@@ -712,8 +712,12 @@ dvs_status dvs_build_index(const dvs_build_params* bp, const float* h_vecs, uint
   if (R == 0 || R > 64) return fail(DVS_ERR_ARG, "R must be in 1..64 for the GPU builder");
   if (L == 0 || L > 1024) return fail(DVS_ERR_ARG, "beam_width must be in 1..1024 for the GPU builder");
   if (bits != 1 && bits != 2 && bits != 4 && bits != 8) return fail(DVS_ERR_BITS, "rabitq_bits must be 1, 2, 4, or 8");
-  if (bp->metric != DVS_METRIC_L2)
-    return fail(DVS_ERR_UNSUPPORTED, "the GPU builder builds L2 graphs; inner-product builds are not available");
+  // An inner-product index (metadata "distance": "ip", searched with the
+  // 1 - dot medoid seed) is built with L2 graph distances.  For unit-norm
+  // vectors, the configuration the reference's IP mode serves, 1 - dot equals
+  // half the squared L2 distance: every ranking, the medoid and RobustPrune's
+  // alpha test (both sides scale by 1/2) are the same, up to rounding.
+  if (bp->metric != DVS_METRIC_L2 && bp->metric != DVS_METRIC_IP) return fail(DVS_ERR_ARG, "metric must be l2 or ip");
   for (uint64_t i = 0; i < n * dim; ++i)
     if (!std::isfinite(h_vecs[i])) return fail(DVS_ERR_ARG, "input vectors contain a non-finite value");
   if (stats) *stats = dvs_build_stats{};

@@ -35,10 +35,12 @@ void dev_free(T*& p) {
 
 // Visited-set sizing.  Without an explicit size the shared-memory table gets
 // between kSlotsMin and kSlotsMax slots per beam entry: the largest size that
-// keeps the most warps resident (48 for the 96-dim L = 64 search, 16 warps per
-// SM; 40 for 960-dim records at L = 200: 7 warps instead of 5).
-// Queries that outgrow it spill to a per-warp table in global memory.
-constexpr uint32_t kSlotsMin = 40;
+// keeps the most warps resident (40 for the 96-dim L = 64 search, 20 warps per
+// SM; 32 for L = 128).  Queries that outgrow it continue in a per-warp table in
+// global memory, which costs little since those tables are reused under
+// epochs instead of cleared (96-dim L = 128: 32 slots, every query spilling,
+// 6.93 ms per 10,000 queries; 48 slots, 22 % spilling, 7.84 ms).
+constexpr uint32_t kSlotsMin = 32;
 constexpr uint32_t kSlotsMax = 48;
 constexpr uint32_t kOverflowSlots = 1u << 14;
 
@@ -66,6 +68,7 @@ struct Device {
   uint32_t* ids = nullptr;
   float* P = nullptr;
   float* c_rot = nullptr;
+  TcRotation tc;          // P split for the tensor-core rotation (made by dvs_set_rotation)
   DevLayout lay;
   // scratch
   size_t q_cap = 0;        // queries the scratch holds
@@ -104,6 +107,7 @@ struct Device {
     dev_free(ids);
     dev_free(P);
     dev_free(c_rot);
+    tc_rotation_release(&tc);
     dev_free(queries);
     dev_free(qrot);
     dev_free(qfac);

@@ -105,7 +105,7 @@ dvs_status noalloc_enqueue(dvs_index* ix, Device& d, const float* d_queries, uin
   DVS_CUDA(cudaMemsetAsync(work, 0, 16, st));
   if (rabitq) {
     if (ix->rotation == DVS_ROTATION_TENSOR)
-      DVS_CUDA(launch_prepare_tc(d_queries, lay.dim, lay.P, lay.c_rot, qrot, lay.vec_stride, qfac, 4, lay.dim,
+      DVS_CUDA(launch_prepare_tc(d_queries, lay.dim, d.tc, lay.c_rot, qrot, lay.vec_stride, qfac, 4, lay.dim,
                                  lay.bits, nq, work + 1, st));
     else
       DVS_CUDA(launch_prepare(d_queries, lay.dim, lay.P, lay.c_rot, qrot, lay.vec_stride, qfac, 4, lay.dim, lay.bits,
@@ -135,7 +135,7 @@ dvs_status noalloc_enqueue(dvs_index* ix, Device& d, const float* d_queries, uin
   a.hlimit = sh.hlimit;
   a.vt16 = sh.vt16;
   a.hbuckets = sh.hbuckets;
-  a.inv_hbuckets = sh.hbuckets ? 1.0f / float(sh.hbuckets) : 0.f;
+  a.hb_magic = sh.hbuckets ? uint32_t(0xFFFFFFFFull / sh.hbuckets + 1) : 0u;
   a.cap_pad = sh.cap_pad;
   a.dim_pad = lay.vec_stride;
   DVS_CUDA(launch_search(a, sh.wpb, blocks, st));

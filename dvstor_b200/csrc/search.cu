@@ -143,15 +143,15 @@ struct Slot16 {
   uint32_t b, tag;
 };
 
-__device__ __forceinline__ Slot16 split16(uint32_t h, uint32_t nb, float inv_nb, uint32_t which) {
-  uint32_t q = __float2uint_rz(__fmul_rz(float(h), inv_nb));
+// (hk mod nb, which << 14 | hk div nb).  The quotient is the high word of
+// hk * magic with magic = ceil(2^32 / nb): for hk < 2^24 it is the exact
+// quotient or one more, which the remainder's sign corrects.
+__device__ __forceinline__ Slot16 split16(uint32_t h, uint32_t nb, uint32_t magic, uint32_t which) {
+  uint32_t q = __umulhi(h, magic);
   int32_t r = int32_t(h) - int32_t(q * nb);
   if (r < 0) {
     --q;
     r += int32_t(nb);
-  } else if (r >= int32_t(nb)) {
-    ++q;
-    r -= int32_t(nb);
   }
   return {uint32_t(r), (which << 14) | q};
 }
@@ -176,11 +176,11 @@ enum : uint32_t { kVisited = 0, kFresh = 1, kNoRoom = 2 };
 
 // Looks `id` up and, when absent and `may_insert`, inserts it.  Returns
 // kVisited, kFresh, or kNoRoom (absent and not insertable here).
-__device__ __forceinline__ uint32_t visit16(uint32_t* tab, uint32_t nb, float inv_nb, uint32_t id, bool may_insert,
+__device__ __forceinline__ uint32_t visit16(uint32_t* tab, uint32_t nb, uint32_t magic, uint32_t id, bool may_insert,
                                             uint32_t w) {
   const uint32_t mask = (1u << w) - 1u;
-  const Slot16 s1 = split16(mixw(id ^ (0x5A5A5Au & mask), w), nb, inv_nb, 0);
-  const Slot16 s2 = split16(mixw(id ^ (0x3C3C3Cu & mask), w), nb, inv_nb, 1);
+  const Slot16 s1 = split16(mixw(id ^ (0x5A5A5Au & mask), w), nb, magic, 0);
+  const Slot16 s2 = split16(mixw(id ^ (0x3C3C3Cu & mask), w), nb, magic, 1);
   unsigned short* t16 = reinterpret_cast<unsigned short*>(tab);
   for (int attempt = 0; attempt < 4; ++attempt) {
     const uint4 v1 = load_bucket(tab, s1.b), v2 = load_bucket(tab, s2.b);
@@ -324,6 +324,15 @@ __device__ __forceinline__ void estimate_quad_chains(const DevLayout& ix, const 
   }
 }
 
+// Asks L2 for every 128-byte line of node g's RaBitQ record (wide records:
+// their chunks are loaded in several dependent batches, which then hit L2).
+__device__ __forceinline__ void prefetch_record_l2(const DevLayout& ix, uint32_t g) {
+  const uintptr_t r = reinterpret_cast<uintptr_t>(rec_row(ix, g));
+  const uintptr_t last = (r + ix.rec_words * 4 - 1) & ~uintptr_t(127);
+  for (uintptr_t line = r & ~uintptr_t(127); line <= last; line += 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(line));
+}
+
 // Exact L2 of `count` rows (slot ids in `rows`) against q, written to `out`;
 // 4 lanes per row, two rows per lane quad (rows i and i + 8), 16 rows per
 // round.  Warp-uniform control flow.
@@ -348,25 +357,69 @@ __device__ __forceinline__ void l2_rows_warp(const DevLayout& ix, const float* _
 }
 
 // RaBitQ estimate of a record already held in registers (RCH 16-byte chunks).
+// 4-bit codes: the chains run in pairs (0,1) and (2,3) on packed two-lane FP32
+// instructions; each lane of a packed FMA is the same fmaf, so every chain
+// sees the reference's sequence of operations.
 template <int BITS, int RCH>
 __device__ __forceinline__ float estimate_regs(const uint4 (&v)[RCH], const DevLayout& ix, const float* __restrict__ qr,
                                                float q_add, float q_k1) {
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, add_o = 0.f, rs_o = 0.f;
+  float add_o = 0.f, rs_o = 0.f;
+  if constexpr (BITS == 4) {
+    float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
+    const float2 neg_magic = make_float2(-8388608.0f, -8388608.0f);
 #pragma unroll
-  for (int t = 0; t < RCH; ++t) {
-    const uint32_t w[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+    for (int t = 0; t < RCH; ++t) {
+      const uint32_t w[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const uint32_t wi = t * 4 + e;
-      if (wi < ix.code_words)
-        code_word<BITS>(w[e], wi, e, ix, qr, s0, s1, s2, s3);
-      else if (wi == ix.code_words)
-        add_o = __uint_as_float(w[e]);
-      else if (wi == ix.code_words + 1)
-        rs_o = __uint_as_float(w[e]);
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t wi = t * 4 + e;
+        if (wi < ix.code_words) {
+          const uint32_t j0 = wi * 8;
+          if (j0 + 8 <= ix.dim) {
+            // nibble n of the word sits in byte n/2 of (n even ? lo : hi); PRMT
+            // places it under the exponent of 2^23, the subtraction leaves it exact
+            const uint32_t lo = w[e] & 0x0F0F0F0Fu, hi = (w[e] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int b = 0; b < 4; b += 2) {
+              const float4 qv = *reinterpret_cast<const float4*>(qr + j0 + 2 * b);
+              const float2 c01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u + b)),
+                                                        __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u + b))),
+                                            neg_magic);
+              const float2 c23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7441u + b)),
+                                                        __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7441u + b))),
+                                            neg_magic);
+              s01 = __ffma2_rn(c01, make_float2(qv.x, qv.y), s01);
+              s23 = __ffma2_rn(c23, make_float2(qv.z, qv.w), s23);
+            }
+          } else {
+            rabitq_word<4>(w[e], qr, j0, ix.dim, s01.x, s01.y, s23.x, s23.y);
+          }
+        } else if (wi == ix.code_words) {
+          add_o = __uint_as_float(w[e]);
+        } else if (wi == ix.code_words + 1) {
+          rs_o = __uint_as_float(w[e]);
+        }
+      }
     }
+    return rabitq_finish(tile4_sum(s01.x, s01.y, s23.x, s23.y), add_o, rs_o, q_add, q_k1, 15.0f);
+  } else {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int t = 0; t < RCH; ++t) {
+      const uint32_t w[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t wi = t * 4 + e;
+        if (wi < ix.code_words)
+          code_word<BITS>(w[e], wi, e, ix, qr, s0, s1, s2, s3);
+        else if (wi == ix.code_words)
+          add_o = __uint_as_float(w[e]);
+        else if (wi == ix.code_words + 1)
+          rs_o = __uint_as_float(w[e]);
+      }
+    }
+    return rabitq_finish(tile4_sum(s0, s1, s2, s3), add_o, rs_o, q_add, q_k1, float((1u << BITS) - 1u));
   }
-  return rabitq_finish(tile4_sum(s0, s1, s2, s3), add_o, rs_o, q_add, q_k1, float((1u << BITS) - 1u));
 }
 
 // Warp-uniform first index p >= lo of a sorted shared array with a[p] >= x.
@@ -386,15 +439,17 @@ __device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n,
 // flight per batch.
 constexpr int kWideRecs = 3, kWideBatch = 6;
 
-// Register cap of a search_kernel instantiation.  R <= 32 with records held in
-// registers: 128, four warps per SM sub-partition (16,384 registers each), so
-// that shared memory (14 warps with the compact visited table at L = 64), not
-// registers, bounds the warps per SM.  Records loaded after the visited check
-// (wider than 128 bytes): 168, three warps per sub-partition (12 per SM, what
-// shared memory allows for 768-dim records at L = 64).  The rest are bounded
-// by shared memory or need their registers, and keep up to 255.
+// Register cap of a search_kernel instantiation.  R <= 32 with records of up
+// to 64 bytes in registers (and exact_gpu): 96, five warps per SM
+// sub-partition (16,384 registers each), so that 20 warps fit an SM when
+// shared memory allows (measured on the 96-dim L = 64 search: 96 registers and
+// a 40-slot table, 2.64 M queries/s; 128 registers and 48 slots, 2.55 M).
+// Records of up to 128 bytes in registers: 128 (at 96 they spill).  Records
+// loaded after the visited check (wider than 128 bytes): 168, three warps per
+// sub-partition.  The rest are bounded by shared memory or need their
+// registers, and keep up to 255.
 __host__ __device__ constexpr int search_max_regs(int npl, int rch, bool exact) {
-  return npl == 1 && (rch > 0 || exact) ? 128 : (rch == 0 && !exact) ? 168 : 255;
+  return npl == 1 && (rch == 4 || exact) ? 96 : npl == 1 && rch == 8 ? 128 : (rch == 0 && !exact) ? 168 : 255;
 }
 
 // EXACT: exact_gpu (exact distances, no records; BITS and RCH unused) or
@@ -464,7 +519,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       if (!a.vt16) htab[4 * hash_slot(ix.medoid, a.hcap >> 2)] = ix.medoid;
     }
     __syncwarp();
-    if (a.vt16 && lane == 0) visit16(htab, a.hbuckets, a.inv_hbuckets, ix.medoid, true, a.vt16);
+    if (a.vt16 && lane == 0) visit16(htab, a.hbuckets, a.hb_magic, ix.medoid, true, a.vt16);
     __syncwarp();
     uint32_t nb = 1, hcount = 1, gcount = 0, H = 0, E = 0, err = 0, scan_from = 0;
     if (nonfinite) {
@@ -516,6 +571,13 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
         const uint32_t j = lane + 32u * s;
         pf[s] = (guess != kEmptySlot && j < R) ? __ldg(adj_row(ix, guess) + j) : kEmptySlot;
       }
+      // wide records: every listed neighbour's record is brought towards L2
+      // now (unless the previous hop already did, for a guessed row)
+      if (RCH == 0 && rabitq && !hit) {
+#pragma unroll
+        for (int s = 0; s < NPL; ++s)
+          if (nbr[s] != kEmptySlot) prefetch_record_l2(ix, nbr[s]);
+      }
       // records of every listed neighbour are requested before the visited
       // check so their latency overlaps it; visited ones are discarded
       uint4 rv[NPL][RCH > 0 ? RCH : 1];
@@ -548,7 +610,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
           if (!in_spill) {
             uint32_t r;
             if (a.vt16) {
-              r = visit16(htab, a.hbuckets, a.inv_hbuckets, id, may_insert, a.vt16);
+              r = visit16(htab, a.hbuckets, a.hb_magic, id, may_insert, a.vt16);
             } else {
               r = may_insert ? (bucket_insert(htab, a.hcap >> 2, id) ? kFresh : kVisited)
                              : (bucket_contains(htab, a.hcap >> 2, id) ? kVisited : kNoRoom);
@@ -644,6 +706,10 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
               cd[i + 8u * k] = rabitq_finish(d, f[k][0], f[k][1], q_add, q_k1, float((1u << BITS) - 1u));
           }
         }
+        // the guessed next row's records, one hop ahead
+#pragma unroll
+        for (int s = 0; s < NPL; ++s)
+          if (pf[s] != kEmptySlot) prefetch_record_l2(ix, pf[s]);
       }
       __syncwarp();
 

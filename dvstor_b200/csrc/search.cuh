@@ -1,6 +1,7 @@
 // Launch-side view of the search kernels (shared by search.cu and api.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -66,7 +67,7 @@ struct SearchArgs {
   uint32_t hcap = 0, hlimit = 0;    // shared-memory visited table: words, entry limit
   uint32_t vt16 = 0;                // compact 16-bit two-choice table: its hash width (20 or 24), 0 = 32-bit table
   uint32_t hbuckets = 0;            // its bucket count (8 entries each)
-  float inv_hbuckets = 0.f;
+  uint32_t hb_magic = 0;            // ceil(2^32 / hbuckets): division by the bucket count as a multiply-high
   uint32_t cap_pad = 0, dim_pad = 0;
   uint32_t out_slots = 0;           // 1: results are dense slots (online insert), else stored node ids
 };
@@ -118,11 +119,25 @@ cudaError_t launch_prepare(const float* queries, uint32_t q_stride, const float*
 cudaError_t launch_query_factors(float* qrot, uint32_t qrot_stride, const float* c_rot, float* qfac,
                                  uint32_t fac_stride, uint32_t dim, uint32_t bits, uint32_t nq, cudaStream_t stream);
 
-// Q' = Q P^T on tcgen05 tensor cores (3xTF32) plus the query factors; a
-// bounded mbarrier wait that expires ORs kErrTimeout into *err.
-cudaError_t launch_prepare_tc(const float* queries, uint32_t q_stride, const float* P, const float* c_rot, float* qrot,
-                              uint32_t qrot_stride, float* qfac, uint32_t fac_stride, uint32_t dim, uint32_t bits,
-                              uint32_t nq, uint32_t* err, cudaStream_t stream);
+// The rotation P split for the tensor cores: tf32 hi and lo planes of dim rows
+// x kp floats (K zero-padded to a multiple of 32) in one allocation, and the
+// TMA descriptors that read them in 32-float x N-tile boxes.
+struct TcRotation {
+  CUtensorMap map_hi, map_lo;
+  float* split = nullptr;
+  uint32_t dim = 0, kp = 0;
+};
+
+// Splits P (on `stream`) into t, replacing what t held; allocates.
+cudaError_t tc_rotation_prepare(const float* P, uint32_t dim, TcRotation* t, cudaStream_t stream);
+void tc_rotation_release(TcRotation* t);
+
+// Q' = Q P^T on tcgen05 tensor cores (3xTF32, P split by tc_rotation_prepare)
+// plus the query factors; a bounded mbarrier wait that expires ORs
+// kErrTimeout into *err.
+cudaError_t launch_prepare_tc(const float* queries, uint32_t q_stride, const TcRotation& t, const float* c_rot,
+                              float* qrot, uint32_t qrot_stride, float* qfac, uint32_t fac_stride, uint32_t dim,
+                              uint32_t bits, uint32_t nq, uint32_t* err, cudaStream_t stream);
 
 // Launches the persistent search kernel; warps_per_block and blocks come from
 // the caller's occupancy computation.

@@ -332,7 +332,8 @@ typedef struct dvs_build_params {
   uint32_t rabitq_bits;
   int32_t seed;               /* --seed, default 1234 in the reference */
   uint32_t num_memory_nodes;  /* shard files to write */
-  dvs_metric metric;          /* L2 only */
+  dvs_metric metric;          /* written to meta.json; the graph uses L2 distances,
+                                 which rank unit-norm vectors as inner product does */
   int device;
   uint32_t batch_cap;         /* 0 = 2% of n (at most 65536) */
   uint32_t visited_cap;       /* per-node visited-set capacity, 0 = 16384 */
