@@ -161,7 +161,6 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool 
   const uint32_t vt16 = d.lay.n < (1u << 20) ? 20u : 24u;
   const uint64_t key = uint64_t(cap) | uint64_t(slots_per_entry) << 24 | uint64_t(exact) << 40 |
                        uint64_t(t16) << 41 | uint64_t(vt16 == 20) << 42;
-  const uint32_t qlayout = search_query_layout(exact, d.lay.bits, d.lay.code_words);
   {
     std::lock_guard<std::mutex> g(g_shape_mu);
     const auto it = d.shapes.find(key);
@@ -182,25 +181,30 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool 
     c.cap_pad = (cap + 31) / 32 * 32;
     if (t16) {
       // 16-bit entries, 8 per 16-byte bucket; at least 2^(W-14) buckets for
-      // hash width W.  The entry limit follows spe even where the bucket
-      // minimum is larger.
+      // hash width W.  Two-choice buckets fill to the last entry: an id spills
+      // only when both its buckets are full.
       c.vt16 = vt16;
       c.hbuckets = std::max(1u << (vt16 - 14), (cap * spe + 7) / 8);
       c.hcap = c.hbuckets * 4;
-      c.hlimit = std::min(c.hbuckets * 8, cap * spe) / 10 * 9;
+      c.hlimit = c.hbuckets * 8;
     } else {
       c.hcap = std::max(64u, (cap * spe + 31) / 32 * 32);
       c.hlimit = c.hcap / 10 * 9;
     }
-    const uint32_t words = search_warp_words(c.cap_pad, d.lay.vec_stride, c.hcap, d.lay.R, qlayout);
+    const bool coop = search_cooperative(exact, d.lay.bits, d.lay.code_words);
     for (uint32_t wpb : {1u, 2u, 4u, 8u}) {
-      const size_t smem = size_t(wpb) * words * 4;
+      if (coop && wpb != 4) continue;  // a query per CTA of four warps
+      const size_t smem = search_block_smem(c.cap_pad, d.lay.vec_stride, c.hcap, d.lay.R, d.lay.rec_words, exact,
+                                            d.lay.bits, d.lay.code_words, wpb);
       if (smem > size_t(kMaxBlockSmem)) break;
       int bps = 0;
       const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, exact, wpb, smem, &bps);
       if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
-      if (int(wpb) * bps > best_warps) {
-        best_warps = int(wpb) * bps;
+      if (bps == 0) break;  // more than a block's shared memory
+      const uint32_t qpb = coop ? 1u : wpb;
+      if (int(qpb) * bps > best_warps) {
+        best_warps = int(qpb) * bps;
+        c.qpb = qpb;
         c.wpb = wpb;
         c.blocks_per_sm = uint32_t(bps);
         best = c;
@@ -257,9 +261,9 @@ dvs_status search_enqueue(dvs_index* ix, Device& d, const float* d_q, uint32_t n
   rc = ensure_scratch(d, nq, k, false);
   if (rc != DVS_OK) return rc;
   const uint32_t blocks_full = s.blocks_per_sm * d.sm_count;
-  const uint32_t blocks_needed = (nq + s.wpb - 1) / s.wpb;
+  const uint32_t blocks_needed = (nq + s.qpb - 1) / s.qpb;
   const uint32_t blocks = std::max(1u, std::min(blocks_full, blocks_needed));
-  const size_t slots = size_t(blocks) * s.wpb;
+  const size_t slots = size_t(blocks) * s.qpb;
   if (slots > d.ovf_slots) {
     // spill tables and their epoch words start zeroed: every entry empty
     dev_free(d.ovf);

@@ -46,6 +46,7 @@ constexpr uint32_t kOverflowSlots = 1u << 14;
 
 struct LaunchShape {
   uint32_t cap = 0, cap_pad = 0, hcap = 0, wpb = 0, blocks_per_sm = 0;
+  uint32_t qpb = 0;  // queries a block serves at once: wpb, or 1 for a cooperative block
   uint32_t vt16 = 0, hbuckets = 0, hlimit = 0;
 };
 

@@ -98,8 +98,8 @@ dvs_status noalloc_enqueue(dvs_index* ix, Device& d, const float* d_queries, uin
   float* qrot = reinterpret_cast<float*>(base + kWorkBytes + kEpochBytes + qfac_bytes);
   uint32_t* tables = reinterpret_cast<uint32_t*>(base + kTablesOffset);
   // one spill table per warp slot: as many blocks as have a table for every warp
-  const uint32_t blocks_needed = (nq + sh.wpb - 1) / sh.wpb;
-  const uint32_t blocks_fit = std::max(1u, kNoAllocTables / sh.wpb);
+  const uint32_t blocks_needed = (nq + sh.qpb - 1) / sh.qpb;
+  const uint32_t blocks_fit = std::max(1u, kNoAllocTables / sh.qpb);
   const uint32_t blocks = std::max(1u, std::min({sh.blocks_per_sm * d.sm_count, blocks_needed, blocks_fit}));
 
   DVS_CUDA(cudaMemsetAsync(work, 0, 16, st));

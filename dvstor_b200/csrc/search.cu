@@ -156,43 +156,48 @@ __device__ __forceinline__ Slot16 split16(uint32_t h, uint32_t nb, uint32_t magi
   return {uint32_t(r), (which << 14) | q};
 }
 
+// Entries hold at most 15 bits, and 0xFFFF is empty, so both tests are exact
+// zero-halfword detections: (x - 0x00010001) & ~x & 0x80008000 sets bit 15 of a
+// halfword iff it is zero, given that a nonzero halfword of x (or of ~v) never
+// has bit 15 clear where the borrow from a zero halfword below could set it.
+__device__ __forceinline__ uint32_t zero_halves(uint32_t x) { return (x - 0x00010001u) & ~x & 0x80008000u; }
+
 __device__ __forceinline__ bool holds16(const uint4& v, uint32_t tag) {
   const uint32_t t = tag * 0x10001u;
-  return (__vcmpeq2(v.x, t) | __vcmpeq2(v.y, t) | __vcmpeq2(v.z, t) | __vcmpeq2(v.w, t)) != 0;
+  return (zero_halves(v.x ^ t) | zero_halves(v.y ^ t) | zero_halves(v.z ^ t) | zero_halves(v.w ^ t)) != 0;
 }
 
-__device__ __forceinline__ uint32_t empty16(const uint4& v) {  // bit e set = entry e empty
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  uint32_t m = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m |= ((w[i] & 0xFFFFu) == 0xFFFFu ? 1u : 0u) << (2 * i);
-    m |= ((w[i] >> 16) == 0xFFFFu ? 1u : 0u) << (2 * i + 1);
-  }
-  return m;
+// Empty entries of a bucket: bit 15 - w (entry 2w) and bit 31 - w (entry 2w + 1).
+__device__ __forceinline__ uint32_t empty16(const uint4& v) {
+  return zero_halves(~v.x) | (zero_halves(~v.y) >> 1) | (zero_halves(~v.z) >> 2) | (zero_halves(~v.w) >> 3);
 }
+
+__device__ __forceinline__ uint32_t empty_entry(uint32_t bit) { return bit >= 16 ? 2 * (31 - bit) + 1 : 2 * (15 - bit); }
 
 enum : uint32_t { kVisited = 0, kFresh = 1, kNoRoom = 2 };
 
-// Looks `id` up and, when absent and `may_insert`, inserts it.  Returns
-// kVisited, kFresh, or kNoRoom (absent and not insertable here).
-__device__ __forceinline__ uint32_t visit16(uint32_t* tab, uint32_t nb, uint32_t magic, uint32_t id, bool may_insert,
-                                            uint32_t w) {
+// Looks `id` up and, when absent and one of its two buckets has a free entry,
+// inserts it.  Returns kVisited, kFresh, or kNoRoom (absent, both buckets
+// full).  Entries are never removed during a query, so an id that was once
+// refused for want of room still finds both its buckets full.
+__device__ __forceinline__ uint32_t visit16(uint32_t* tab, uint32_t nb, uint32_t magic, uint32_t id, uint32_t w) {
   const uint32_t mask = (1u << w) - 1u;
-  const Slot16 s1 = split16(mixw(id ^ (0x5A5A5Au & mask), w), nb, magic, 0);
-  const Slot16 s2 = split16(mixw(id ^ (0x3C3C3Cu & mask), w), nb, magic, 1);
+  // the second hash is an odd multiple of the first modulo 2^w: a bijection of it, hence of the id
+  const uint32_t h1 = mixw(id ^ (0x5A5A5Au & mask), w);
+  const Slot16 s1 = split16(h1, nb, magic, 0);
+  const Slot16 s2 = split16((h1 * 0x2C1B3Du) & mask, nb, magic, 1);
   unsigned short* t16 = reinterpret_cast<unsigned short*>(tab);
-  for (int attempt = 0; attempt < 4; ++attempt) {
+  // a failed claim means another lane filled an entry of these buckets: at most 16 can
+  for (int attempt = 0; attempt < 17; ++attempt) {
     const uint4 v1 = load_bucket(tab, s1.b), v2 = load_bucket(tab, s2.b);
     if (holds16(v1, s1.tag) || holds16(v2, s2.tag)) return kVisited;
-    if (!may_insert) return kNoRoom;
     const uint32_t e1 = empty16(v1), e2 = empty16(v2);
     if ((e1 | e2) == 0) return kNoRoom;
     const bool first = __popc(e1) >= __popc(e2);
     uint32_t em = first ? e1 : e2;
     const Slot16 c = first ? s1 : s2;
     while (em) {
-      const uint32_t e = __ffs(em) - 1;
+      const uint32_t e = empty_entry(__ffs(em) - 1);
       em &= em - 1;
       const unsigned short old = atomicCAS(t16 + 8 * c.b + e, (unsigned short)0xFFFF, (unsigned short)c.tag);
       if (old == 0xFFFF) return kFresh;
@@ -448,8 +453,150 @@ constexpr int kWideRecs = 3, kWideBatch = 6;
 // loaded after the visited check (wider than 128 bytes): 168, three warps per
 // sub-partition.  The rest are bounded by shared memory or need their
 // registers, and keep up to 255.
-__host__ __device__ constexpr int search_max_regs(int npl, int rch, bool exact) {
-  return npl == 1 && (rch == 4 || exact) ? 96 : npl == 1 && rch == 8 ? 128 : (rch == 0 && !exact) ? 168 : 255;
+// Records wider than 128 bytes with 1/2/4-bit codes run cooperatively (a
+// query per CTA of 4 warps, estimates from shared memory): 128, four CTAs per
+// SM.
+__host__ __device__ constexpr bool search_coop(int bits, int rch, bool exact) { return rch == 0 && !exact && bits != 8; }
+
+__host__ __device__ constexpr int search_max_regs(int bits, int npl, int rch, bool exact) {
+  return search_coop(bits, rch, exact)         ? 128
+         : npl == 1 && (rch == 4 || exact)     ? 96
+         : npl == 1 && rch == 8                ? 128
+         : (rch == 0 && !exact)                ? 168
+                                               : 255;
+}
+
+// ---- cooperative wide-record search: a query per CTA of 4 warps ----
+// Warp 0 (the leader) runs the whole Vamana loop as a search warp does; the
+// other three warps join it only for the two wide phases, the estimates of an
+// expansion's fresh neighbours and the final rerank, through named barrier 1.
+// The records of every listed neighbour are fetched into a shared-memory
+// stage by one bulk copy each (this GPU's or a peer's memory, no multicast)
+// while the leader filters the visited set, so an expansion waits for one
+// memory round trip instead of a load batch per few chunks.
+constexpr uint32_t kCoopWarps = 4;
+constexpr uint32_t kCmdExit = 0, kCmdEstimate = 1, kCmdRerank = 2;
+constexpr uint32_t kCoopCtlWords = 8;  // cmd, count, q_add, q_k1, stage parity, pad; then the fresh list's row positions
+constexpr uint32_t kCoopWaitLimit = 1u << 22;
+
+__device__ __forceinline__ void coop_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool stage_wait(uint32_t mbar, uint32_t parity) {
+  for (uint32_t it = 0; it < kCoopWaitLimit; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(mbar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+// Chain t of two records' estimates (lane t of a lane quad, the reference
+// kernel's tile split: dims j = t mod 4 in ascending order), from records in
+// shared memory; the two chains run on packed two-lane FMAs sharing each q'
+// value.  `q` is this lane's chain of the chain-major q'.
+template <int BITS>
+__device__ __forceinline__ float2 estimate_pair_smem(const uint32_t* rA, const uint32_t* rB, uint32_t dim,
+                                                     const float* __restrict__ q, uint32_t t) {
+  constexpr uint32_t kPer = 32 / BITS, kMask = (1u << BITS) - 1u;
+  const float2 nm = make_float2(-8388608.0f, -8388608.0f);
+  const uint32_t nch = (dim / kPer) >> 2;  // chunks whose every dim is < dim
+  const uint32_t sh0 = BITS * t;
+  float2 s = make_float2(0.f, 0.f);
+  for (uint32_t ch = 0; ch < nch; ++ch) {
+    const uint4 va = reinterpret_cast<const uint4*>(rA)[ch];
+    const uint4 vb = reinterpret_cast<const uint4*>(rB)[ch];
+    float qf[kPer];
+    const float4* q4 = reinterpret_cast<const float4*>(q + ch * kPer);
+#pragma unroll
+    for (uint32_t g = 0; g < kPer / 4; ++g) {
+      const float4 f = q4[g];
+      qf[4 * g] = f.x;
+      qf[4 * g + 1] = f.y;
+      qf[4 * g + 2] = f.z;
+      qf[4 * g + 3] = f.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t wa = e == 0 ? va.x : e == 1 ? va.y : e == 2 ? va.z : va.w;
+      const uint32_t wb = e == 0 ? vb.x : e == 1 ? vb.y : e == 2 ? vb.z : vb.w;
+#pragma unroll
+      for (uint32_t i = 0; i < kPer / 4; ++i) {
+        const uint32_t sh = sh0 + 4 * BITS * i;
+        const float qv = qf[e * (kPer / 4) + i];
+        const float2 c = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | ((wa >> sh) & kMask)),
+                                                __uint_as_float(0x4B000000u | ((wb >> sh) & kMask))),
+                                    nm);
+        s = __ffma2_rn(c, make_float2(qv, qv), s);
+      }
+    }
+  }
+  // words past the last whole chunk, the partial last word included
+  for (uint32_t wi = nch * 4; wi * kPer < dim; ++wi) {
+    const uint32_t wa = rA[wi], wb = rB[wi], j0 = wi * kPer;
+    for (uint32_t n = t; n < kPer && j0 + n < dim; n += 4) {
+      const float qv = q[(j0 + n) >> 2];
+      const float2 c = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | ((wa >> (BITS * n)) & kMask)),
+                                              __uint_as_float(0x4B000000u | ((wb >> (BITS * n)) & kMask))),
+                                  nm);
+      s = __ffma2_rn(c, make_float2(qv, qv), s);
+    }
+  }
+  return s;
+}
+
+// This warp's share of the estimates of the m fresh neighbours (m <= 64):
+// lane quad g = warp * 8 + lane / 4 of the CTA takes candidates g and g + 32,
+// whose records sit in the stage at their adjacency-row positions.
+template <int BITS>
+__device__ __forceinline__ void coop_estimate(const DevLayout& ix, const uint32_t* stage, const uint32_t* cpos,
+                                              uint32_t m, const float* qr, uint32_t cs, float q_add, float q_k1,
+                                              float* cd, uint32_t wib, uint32_t lane) {
+  const uint32_t t = lane & 3, g = wib * 8 + (lane >> 2);
+  const uint32_t iA = g, iB = g + 32;
+  const uint32_t* rA = stage + size_t(iA < m ? cpos[iA] : 0) * ix.rec_words;
+  const uint32_t* rB = stage + size_t(iB < m ? cpos[iB] : 0) * ix.rec_words;
+  const float2 p = estimate_pair_smem<BITS>(rA, rB, ix.dim, qr + t * cs, t);
+  const float dA = quad_butterfly(p.x), dB = quad_butterfly(p.y);
+  if (t == 0) {
+    constexpr float k1 = float((1u << BITS) - 1u);
+    if (iA < m)
+      cd[iA] = rabitq_finish(dA, __uint_as_float(rA[ix.code_words]), __uint_as_float(rA[ix.code_words + 1]), q_add,
+                             q_k1, k1);
+    if (iB < m)
+      cd[iB] = rabitq_finish(dB, __uint_as_float(rB[ix.code_words]), __uint_as_float(rB[ix.code_words + 1]), q_add,
+                             q_k1, k1);
+  }
+}
+
+// This warp's rounds of the exact rerank of `count` beam rows (the round body
+// of l2_rows_warp; warp w takes rounds w, w + 4, ...).
+__device__ __forceinline__ void coop_rerank(const DevLayout& ix, const float* __restrict__ q, const uint32_t* rows,
+                                            uint32_t count, float* out, uint32_t lane, uint32_t wib) {
+  const uint32_t t = lane & 3;
+  for (uint32_t r0 = 16 * wib; r0 < count; r0 += 16 * kCoopWarps) {
+    const uint32_t iA = r0 + (lane >> 2), iB = iA + 8;
+    float pA = 0.f, pB = 0.f;
+    if (iA < count) {
+      const float* xA = vec_row(ix, rows[iA] & ~kExpandedBit);
+      const float* xB = iB < count ? vec_row(ix, rows[iB] & ~kExpandedBit) : xA;
+      l2_quad_partial2(q, xA, xB, ix.dim, t, pA, pB);
+    }
+    const float tA = quad_butterfly(pA), tB = quad_butterfly(pB);
+    if (t == 0) {
+      if (iA < count) out[iA] = tA;
+      if (iB < count) out[iB] = tB;
+    }
+  }
 }
 
 // EXACT: exact_gpu (exact distances, no records; BITS and RCH unused) or
@@ -457,12 +604,14 @@ __host__ __device__ constexpr int search_max_regs(int npl, int rch, bool exact) 
 // chunks of a RaBitQ record a lane holds in registers (0 = records too large:
 // they are loaded after the visited check instead).
 template <int BITS, int NPL, int RCH, bool EXACT>
-__global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(const SearchArgs a) {
+__global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint32_t smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const DevLayout& ix = a.ix;
   constexpr uint32_t qlayout = EXACT ? kQueryRaw : (RCH == 0 && BITS != 8 ? kQueryChain : kQueryRot);
-  uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R, qlayout);
+  constexpr bool COOP = search_coop(BITS, RCH, EXACT);
+  const uint32_t warp_words = search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R, qlayout);
+  uint32_t* base = smem + (COOP ? 0 : size_t(wib) * warp_words);
   float* bd = reinterpret_cast<float*>(base);  // the beam: distances
   uint32_t* bi = base + a.cap_pad;            // and slot | expanded bit
   // exact_gpu: the query (qv); rabitq_gpu: q' (qr) in dimension or chain order
@@ -474,12 +623,48 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
   float* sd = reinterpret_cast<float*>(cid + 64 * NPL);
   uint32_t* sid = cid + 96 * NPL;
   uint32_t* htab = cid + 128 * NPL;
-  const uint32_t warp_slot = blockIdx.x * (blockDim.x >> 5) + wib;
+  const uint32_t warp_slot = COOP ? blockIdx.x : blockIdx.x * (blockDim.x >> 5) + wib;
   uint32_t* gtab = a.ovf ? a.ovf + size_t(warp_slot) * a.ovf_cap : nullptr;
   constexpr bool rabitq = !EXACT;  // the mode is a template parameter: each kernel holds one loop body
   const uint32_t dim = ix.dim, R = ix.R;
   const uint32_t nch = (ix.code_words + 2 + 3) >> 2;
   const float kInf = __int_as_float(0x7F800000);
+  // cooperative: the record stage (a record per adjacency-row position), the
+  // control words and the fresh candidates' row positions follow the leader's words
+  uint32_t* stage = smem + warp_words;
+  volatile uint32_t* ctl = stage + size_t(ix.R) * ix.rec_words;
+  uint32_t* cpos = const_cast<uint32_t*>(ctl) + kCoopCtlWords;
+  __shared__ __align__(8) uint64_t stage_bar;
+  uint32_t stage_uses = 0;  // leader: bulk-copy rounds started on stage_bar
+  if constexpr (COOP) {
+    if (threadIdx.x == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&stage_bar)));
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (wib > 0) {
+      // helper warps: estimates and rerank rounds when the leader asks, until it says exit
+      const float* qr_l = reinterpret_cast<const float*>(base + 2 * a.cap_pad);
+      const uint32_t cs_l = chain_stride(a.dim_pad);
+      uint32_t* cid_l = base + 2 * a.cap_pad + 4 * cs_l;
+      float* cd_l = reinterpret_cast<float*>(cid_l + 32 * NPL);
+      for (;;) {
+        coop_sync();
+        const uint32_t cmd = ctl[0];
+        if (cmd == kCmdExit) return;
+        if (cmd == kCmdEstimate) {
+          stage_wait(smem_addr(&stage_bar), ctl[4]);  // already complete: orders the copies before the reads
+          coop_estimate<BITS == 8 ? 4 : BITS>(ix, stage, cpos, ctl[1], qr_l, cs_l, __uint_as_float(ctl[2]),
+                                              __uint_as_float(ctl[3]), cd_l, wib, lane);
+        } else {
+          // the leader put the query into its visited-table words
+          coop_rerank(ix, reinterpret_cast<const float*>(cid_l + 128 * NPL), base + a.cap_pad, ctl[1],
+                      reinterpret_cast<float*>(base), lane, wib);
+        }
+        coop_sync();
+      }
+    }
+  }
 
   for (;;) {
     uint32_t qi = 0;
@@ -519,7 +704,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       if (!a.vt16) htab[4 * hash_slot(ix.medoid, a.hcap >> 2)] = ix.medoid;
     }
     __syncwarp();
-    if (a.vt16 && lane == 0) visit16(htab, a.hbuckets, a.hb_magic, ix.medoid, true, a.vt16);
+    if (a.vt16 && lane == 0) visit16(htab, a.hbuckets, a.hb_magic, ix.medoid, a.vt16);
     __syncwarp();
     uint32_t nb = 1, hcount = 1, gcount = 0, H = 0, E = 0, err = 0, scan_from = 0;
     if (nonfinite) {
@@ -571,9 +756,30 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
         const uint32_t j = lane + 32u * s;
         pf[s] = (guess != kEmptySlot && j < R) ? __ldg(adj_row(ix, guess) + j) : kEmptySlot;
       }
-      // wide records: every listed neighbour's record is brought towards L2
-      // now (unless the previous hop already did, for a guessed row)
-      if (RCH == 0 && rabitq && !hit) {
+      if constexpr (COOP) {
+        // every listed neighbour's record into the stage, at its row position
+        uint32_t nvalid = 0;
+#pragma unroll
+        for (int s = 0; s < NPL; ++s) nvalid += __popc(__ballot_sync(kFull, nbr[s] != kEmptySlot));
+        const uint32_t rbytes = ix.rec_words * 4;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (lane == 0)
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&stage_bar)),
+                       "r"(nvalid * rbytes)
+                       : "memory");
+        __syncwarp();
+#pragma unroll
+        for (int s = 0; s < NPL; ++s)
+          if (nbr[s] != kEmptySlot)
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                    smem_addr(stage + size_t(lane + 32u * s) * ix.rec_words)),
+                "l"(rec_row(ix, nbr[s])), "r"(rbytes), "r"(smem_addr(&stage_bar))
+                : "memory");
+        ++stage_uses;
+      } else if (RCH == 0 && rabitq && !hit) {
+        // wide records: every listed neighbour's record is brought towards L2
+        // now (unless the previous hop already did, for a guessed row)
 #pragma unroll
         for (int s = 0; s < NPL; ++s)
           if (nbr[s] != kEmptySlot) prefetch_record_l2(ix, nbr[s]);
@@ -603,18 +809,20 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
         const uint32_t id = nbr[s];
         const uint32_t peers = __match_any_sync(kFull, id);
         const bool first = id != kEmptySlot && (peers & lanemask_lt()) == 0;
-        const bool may_insert = hcount + 32 <= a.hlimit;
         bool full = false;
         if (first) {
-          const bool in_spill = overflow && table_contains(gtab, a.ovf_cap, id, gtag);
-          if (!in_spill) {
-            uint32_t r;
-            if (a.vt16) {
-              r = visit16(htab, a.hbuckets, a.hb_magic, id, may_insert, a.vt16);
-            } else {
-              r = may_insert ? (bucket_insert(htab, a.hcap >> 2, id) ? kFresh : kVisited)
-                             : (bucket_contains(htab, a.hcap >> 2, id) ? kVisited : kNoRoom);
-            }
+          if (a.vt16) {
+            // an id in the spill table found both its buckets full when it
+            // spilled, and they still are: only such a lookup probes the spill
+            uint32_t r = visit16(htab, a.hbuckets, a.hb_magic, id, a.vt16);
+            if (r == kNoRoom && overflow && table_contains(gtab, a.ovf_cap, id, gtag)) r = kVisited;
+            fresh[s] = r == kFresh;
+            full = r == kNoRoom;
+          } else if (!(overflow && table_contains(gtab, a.ovf_cap, id, gtag))) {
+            // the 32-bit table is linear-probed: it stops taking ids at its load limit
+            const bool may_insert = hcount + 32 <= a.hlimit;
+            const uint32_t r = may_insert ? (bucket_insert(htab, a.hcap >> 2, id) ? kFresh : kVisited)
+                                          : (bucket_contains(htab, a.hcap >> 2, id) ? kVisited : kNoRoom);
             fresh[s] = r == kFresh;
             full = r == kNoRoom;
           }
@@ -656,6 +864,11 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
         m += cnt;
         hcount += cnt;
       }
+      if constexpr (COOP) {
+        // the stage's copies land before anything else happens to it
+        if (!stage_wait(smem_addr(&stage_bar), (stage_uses - 1) & 1)) err |= kErrTimeout;
+        if (err & kErrTimeout) break;
+      }
       if (err & kErrCapacity) break;
       if (m == 0) {
         scan_from = best + 1;
@@ -672,6 +885,7 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
           if (fresh[s]) {
             const uint32_t pos = base_pos + __popc(bal & lanemask_lt());
             cid[pos] = nbr[s];
+            if (COOP) cpos[pos] = lane + 32u * s;
             if (RCH > 0 && rabitq) cd[pos] = estimate_regs<BITS, (RCH > 0 ? RCH : 1)>(rv[s], ix, qr, q_add, q_k1);
           }
           base_pos += __popc(bal);
@@ -680,6 +894,18 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       __syncwarp();
       if (!rabitq) {
         l2_rows_warp(ix, qv, cid, m, cd, lane, 0xFFFFFFFFu);
+      } else if (COOP) {
+        if (lane == 0) {
+          ctl[0] = kCmdEstimate;
+          ctl[1] = m;
+          ctl[2] = __float_as_uint(q_add);
+          ctl[3] = __float_as_uint(q_k1);
+          ctl[4] = (stage_uses - 1) & 1;
+        }
+        __syncwarp();
+        coop_sync();
+        coop_estimate<BITS == 8 ? 4 : BITS>(ix, stage, cpos, m, qr, cs, q_add, q_k1, cd, 0, lane);
+        coop_sync();
       } else if (RCH == 0) {
         // wide records: 8 * kWideRecs per round, kWideRecs per lane quad
         // (candidates i, i + 8, ...), chains reduced with the tile butterfly
@@ -827,7 +1053,18 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       __syncwarp();
       for (uint32_t j = lane; j < a.dim_pad; j += 32) qx[j] = j < dim ? qg[j] : 0.f;
       __syncwarp();
-      l2_rows_warp(ix, qx, bi, nb, bd, lane, ~kExpandedBit);
+      if constexpr (COOP) {
+        if (lane == 0) {
+          ctl[0] = kCmdRerank;
+          ctl[1] = nb;
+        }
+        __syncwarp();
+        coop_sync();
+        coop_rerank(ix, qx, bi, nb, bd, lane, 0);
+        coop_sync();
+      } else {
+        l2_rows_warp(ix, qx, bi, nb, bd, lane, ~kExpandedBit);
+      }
       Cr = nb;
       __syncwarp();
       for (uint32_t p = lane; p < nb; p += 32) {
@@ -864,6 +1101,12 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       if (overflow) atomicAdd(a.work + 2, 1u);
     }
     __syncwarp();
+  }
+  if constexpr (COOP) {
+    // the helper warps leave with the leader
+    if (lane == 0) ctl[0] = kCmdExit;
+    __syncwarp();
+    coop_sync();
   }
 }
 
@@ -932,14 +1175,21 @@ __global__ void l2_rows_kernel(const float* __restrict__ q, const float* __restr
 
 template <int BITS, int NPL, int RCH, bool EXACT>
 cudaError_t occ(uint32_t wpb, size_t smem, int* bps) {
-  // the largest allowance once for all shapes, so concurrent searches of other
-  // shapes never find it lowered under them
-  (void)smem;
-  cudaError_t e = cudaFuncSetAttribute(search_kernel<BITS, NPL, RCH, EXACT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxBlockSmem);
+  // the largest allowance once for all shapes (a block's static and dynamic
+  // shared memory together at most kMaxBlockSmem), so concurrent searches of
+  // other shapes never find it lowered under them
+  auto* k = search_kernel<BITS, NPL, RCH, EXACT>;
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, k);
   if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(bps, search_kernel<BITS, NPL, RCH, EXACT>, int(wpb * 32),
-                                                       smem);
+  const size_t max_dynamic = size_t(kMaxBlockSmem) - fa.sharedSizeBytes;
+  e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(max_dynamic));
+  if (e != cudaSuccess) return e;
+  if (smem > max_dynamic) {
+    *bps = 0;
+    return cudaSuccess;
+  }
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(bps, k, int(wpb * 32), smem);
 }
 
 template <int BITS, int NPL, int RCH, bool EXACT>
@@ -994,11 +1244,21 @@ cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, boo
   }
 }
 
+bool search_cooperative(bool exact, uint32_t bits, uint32_t code_words) {
+  return search_coop(int(bits), record_chunks(code_words), exact);
+}
+
+size_t search_block_smem(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R, uint32_t rec_words,
+                         bool exact, uint32_t bits, uint32_t code_words, uint32_t wpb) {
+  const size_t words = search_warp_words(cap_pad, dim_pad, hcap, R, search_query_layout(exact, bits, code_words));
+  if (search_cooperative(exact, bits, code_words))  // one query: leader words, record stage, control, positions
+    return (words + size_t(R) * rec_words + kCoopCtlWords + 64) * 4;
+  return size_t(wpb) * words * 4;
+}
+
 cudaError_t launch_search(const SearchArgs& a, uint32_t wpb, uint32_t blocks, cudaStream_t stream) {
-  const size_t smem = size_t(wpb) *
-                     search_warp_words(a.cap_pad, a.dim_pad, a.hcap, a.ix.R,
-                                       search_query_layout(a.mode == 1, a.ix.bits, a.ix.code_words)) *
-                     4;
+  const size_t smem = search_block_smem(a.cap_pad, a.dim_pad, a.hcap, a.ix.R, a.ix.rec_words, a.mode == 1, a.ix.bits,
+                                        a.ix.code_words, wpb);
   const bool two = a.ix.R > 32;
   const int rch = record_chunks(a.ix.code_words);
   const dim3 grid(blocks), block(wpb * 32);
