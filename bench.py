@@ -72,6 +72,8 @@ def parse_args():
     ap.add_argument("--alpha", type=float, default=1.2)
     ap.add_argument("--placement", choices=["replicate", "shard"], default="replicate",
                     help="shard: one process over --gpus devices, the index split by slot (run without torchrun)")
+    ap.add_argument("--rotation", choices=["exact", "tensor"], default="exact",
+                    help="query rotation: fp32 in the oracle's fixed order, or tcgen05 tensor cores (3xTF32)")
     ap.add_argument("--metric", choices=["l2", "ip"], default=None,
                     help="index metric (default: ip for --mode mixed, else l2)")
     ap.add_argument("--clients", type=int, default=16, help="--mode mixed: client threads per GPU")
@@ -265,12 +267,31 @@ def recall(ids, gt):
     return float(np.mean([len(set(ids[i][:k].tolist()) & set(gt[i].tolist())) / k for i in range(len(gt))]))
 
 
-def parity_check(ix, orc, Q, k, L, mode, device):
+def tensor_rotated(ix, Q, device):
+    """The rotated queries and factors the tensor-core rotation gives for this
+    index (dvs_query_prepare_tc with the index's P and rotated centroid)."""
+    import torch
+
+    from dvstor_b200._lib import check, lib, ptr
+
+    P, c = ix.artifacts()
+    dev = f"cuda:{device}"
+    dQ, dP, dc = (torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in (Q, P, c))
+    qr = torch.empty(Q.shape, dtype=torch.float32, device=dev)
+    fac = torch.empty((Q.shape[0], 3), dtype=torch.float32, device=dev)
+    check(lib().dvs_query_prepare_tc(ptr(dQ), ptr(dP), ptr(dc), ptr(qr), ptr(fac), Q.shape[0], Q.shape[1],
+                                     ix.info.rabitq_bits, None))
+    torch.cuda.synchronize(device)
+    return qr.cpu().numpy(), fac.cpu().numpy()
+
+
+def parity_check(ix, orc, Q, k, L, mode, device, rotation="exact"):
     """The GPU search against the oracle's Vamana::knn (src/vamana/vamana.hh:57-452)
     on the same index files and queries: a query matches when its distances are
     equal bit for bit, its expansions H, estimates E and reranked rows C_r are
     equal, and its ids are equal except inside groups of exactly equal final
-    distance (std::sort leaves their order unspecified)."""
+    distance (std::sort leaves their order unspecified).  With the tensor-core
+    rotation the oracle is given the GPU's rotated queries and factors."""
     import torch
 
     nq = Q.shape[0]
@@ -286,7 +307,11 @@ def parity_check(ix, orc, Q, k, L, mode, device):
     g_c = c_t.cpu().numpy().view(np.uint32)
     cap = L + 64 if mode == "rabitq_gpu" else L
     t = time.perf_counter()
-    o_ids, o_d, o_c, b_ids, b_d = orc.knn(Q, k, L, mode, beam_cap=cap, threads=os.cpu_count() or 1)
+    q_rot = fac = None
+    if rotation == "tensor" and mode == "rabitq_gpu":
+        q_rot, fac = tensor_rotated(ix, Q, device)
+    o_ids, o_d, o_c, b_ids, b_d = orc.knn(Q, k, L, mode, q_rot=q_rot, factors=fac, beam_cap=cap,
+                                          threads=os.cpu_count() or 1)
     oracle_s = time.perf_counter() - t
     mism, ties = 0, 0
     for q in range(nq):
@@ -300,8 +325,10 @@ def parity_check(ix, orc, Q, k, L, mode, device):
                 else:
                     ok = False
         mism += 0 if ok else 1
-    return {"queries": nq, "mismatches": mism, "tie_diffs": ties, "oracle_s": round(oracle_s, 2),
-            "rule": "distances and H/E/C_r equal bit for bit, ids equal outside exact-distance ties"}
+    rule = "distances and H/E/C_r equal bit for bit, ids equal outside exact-distance ties"
+    if q_rot is not None:
+        rule += "; the oracle given the GPU's tensor-core rotated queries"
+    return {"queries": nq, "mismatches": mism, "tie_diffs": ties, "oracle_s": round(oracle_s, 2), "rule": rule}
 
 
 def index_device_bytes(info):
@@ -457,6 +484,7 @@ def run_ours(args):
     B = args.batch
     prefix = ensure_index(args, wp, device, dist)
     ix = D.Index(prefix, devices=(device,))
+    ix.set_rotation(args.rotation)
     info = ix.info
     nsteps = args.warmup + args.steps
     Qpool = datasets.queries_for(args.workload, B * nsteps, stream=dist.rank)
@@ -542,7 +570,7 @@ def run_ours(args):
         gt = ground_truth(Xv, gtq, k, device)
         rec = recall(g_ids, gt)
         if args.parity_queries:
-            par = parity_check(ix, X, Qpool[:args.parity_queries], k, L, args.search_mode, device)
+            par = parity_check(ix, X, Qpool[:args.parity_queries], k, L, args.search_mode, device, args.rotation)
         if not args.no_cpu_baseline:
             cpu = cpu_baseline(X, np.concatenate([gtq, Qpool[1000:]]), L, k, args.cpu_seconds, gt_q=None)
             ids_cpu, _ = O.cpu_beam_search_batch(X.X, X.adj, X.medoid, gtq, L, k)
@@ -555,7 +583,8 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"],
                        "build_L": wp["build_L"], "rabitq_bits": args.bits, "search_mode": args.search_mode, "k": k,
-                       "beam_width": L, "queries_per_step_per_gpu": B, "parallelism": f"replicas x{dist.world}",
+                       "beam_width": L, "rotation": args.rotation, "queries_per_step_per_gpu": B,
+                       "parallelism": f"replicas x{dist.world}",
                        "l2": f"index {index_device_bytes(info) / 1e9:.2f} GB larger than L2, not flushed; "
                              "fresh query batch every step"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

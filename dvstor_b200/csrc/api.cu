@@ -36,11 +36,8 @@ dvs_status upload(Device& d, const HostIndex& h, uint32_t shard, uint32_t nshard
   int sms = 0;
   DVS_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d.ordinal));
   d.sm_count = uint32_t(sms);
-  DVS_CUDA(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
-  DVS_CUDA(cudaEventCreate(&d.ev0));
-  DVS_CUDA(cudaEventCreate(&d.ev1));
-  DVS_CUDA(cudaEventCreateWithFlags(&d.done, cudaEventDisableTiming));
-  DVS_CUDA(cudaEventRecord(d.done, d.stream));
+  DVS_CUDA(d.sc.create());
+  DVS_CUDA(d.ins.create());
   // records: reference layout -> [codes | pad to word | add | rescale | pad to 16 B]
   std::vector<uint32_t> rec(size_t(nl) * rec_words, 0u);
   std::vector<uint32_t> adj(size_t(nl) * R);
@@ -66,7 +63,6 @@ dvs_status upload(Device& d, const HostIndex& h, uint32_t shard, uint32_t nshard
   DVS_CUDA(cudaMemcpy(d.ids, h.ids.data(), size_t(n) * 4, cudaMemcpyHostToDevice));
   DVS_CUDA(cudaMemcpy(d.P, h.rotation.data(), size_t(dim) * dim * 4, cudaMemcpyHostToDevice));
   DVS_CUDA(cudaMemcpy(d.c_rot, h.rotated_centroid.data(), size_t(dim) * 4, cudaMemcpyHostToDevice));
-  DVS_CUDA(cudaMalloc(&d.work, 16));
   d.shard = shard;
   d.rows = nl;
   d.cap_rows = nl;
@@ -127,27 +123,27 @@ dvs_status link_shards(std::vector<Device>& devs) {
 
 }  // namespace
 
-dvs_status ensure_scratch(Device& d, size_t nq, size_t k, bool host_path) {
+dvs_status ensure_scratch(Device& d, Scratch& sc, size_t nq, size_t k, bool host_path) {
   const size_t vs = d.lay.vec_stride;
-  if (nq > d.q_cap) {
-    const size_t cap = std::max(nq, d.q_cap * 2);
-    dev_free(d.queries);
-    dev_free(d.qrot);
-    dev_free(d.qfac);
-    dev_free(d.counters);
-    DVS_CUDA(cudaMalloc(&d.queries, cap * d.lay.dim * 4));
-    DVS_CUDA(cudaMalloc(&d.qrot, cap * vs * 4));
-    DVS_CUDA(cudaMalloc(&d.qfac, cap * 16));
-    DVS_CUDA(cudaMalloc(&d.counters, cap * 16));
-    d.q_cap = cap;
+  if (nq > sc.q_cap) {
+    const size_t cap = std::max(nq, sc.q_cap * 2);
+    dev_free(sc.queries);
+    dev_free(sc.qrot);
+    dev_free(sc.qfac);
+    dev_free(sc.counters);
+    DVS_CUDA(cudaMalloc(&sc.queries, cap * d.lay.dim * 4));
+    DVS_CUDA(cudaMalloc(&sc.qrot, cap * vs * 4));
+    DVS_CUDA(cudaMalloc(&sc.qfac, cap * 16));
+    DVS_CUDA(cudaMalloc(&sc.counters, cap * 16));
+    sc.q_cap = cap;
   }
-  if (host_path && nq * k > d.out_cap) {
-    const size_t cap = std::max(nq * k, d.out_cap * 2);
-    dev_free(d.out_ids);
-    dev_free(d.out_dist);
-    DVS_CUDA(cudaMalloc(&d.out_ids, cap * 4));
-    DVS_CUDA(cudaMalloc(&d.out_dist, cap * 4));
-    d.out_cap = cap;
+  if (host_path && nq * k > sc.out_cap) {
+    const size_t cap = std::max(nq * k, sc.out_cap * 2);
+    dev_free(sc.out_ids);
+    dev_free(sc.out_dist);
+    DVS_CUDA(cudaMalloc(&sc.out_ids, cap * 4));
+    DVS_CUDA(cudaMalloc(&sc.out_dist, cap * 4));
+    sc.out_cap = cap;
   }
   return DVS_OK;
 }
@@ -191,20 +187,16 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool 
       c.hcap = std::max(64u, (cap * spe + 31) / 32 * 32);
       c.hlimit = c.hcap / 10 * 9;
     }
-    const bool coop = search_cooperative(exact, d.lay.bits, d.lay.code_words);
     for (uint32_t wpb : {1u, 2u, 4u, 8u}) {
-      if (coop && wpb != 4) continue;  // a query per CTA of four warps
-      const size_t smem = search_block_smem(c.cap_pad, d.lay.vec_stride, c.hcap, d.lay.R, d.lay.rec_words, exact,
-                                            d.lay.bits, d.lay.code_words, wpb);
+      const size_t smem =
+          search_block_smem(c.cap_pad, d.lay.vec_stride, c.hcap, d.lay.R, exact, d.lay.bits, d.lay.code_words, wpb);
       if (smem > size_t(kMaxBlockSmem)) break;
       int bps = 0;
       const cudaError_t e = search_occupancy(d.lay.bits, d.lay.R, d.lay.code_words, exact, wpb, smem, &bps);
       if (e != cudaSuccess) return fail(DVS_ERR_CUDA, std::string("occupancy query: ") + cudaGetErrorString(e));
       if (bps == 0) break;  // more than a block's shared memory
-      const uint32_t qpb = coop ? 1u : wpb;
-      if (int(qpb) * bps > best_warps) {
-        best_warps = int(qpb) * bps;
-        c.qpb = qpb;
+      if (int(wpb) * bps > best_warps) {
+        best_warps = int(wpb) * bps;
         c.wpb = wpb;
         c.blocks_per_sm = uint32_t(bps);
         best = c;
@@ -226,72 +218,72 @@ dvs_status launch_shape(Device& d, uint32_t cap, uint32_t slots_per_entry, bool 
 namespace dvs {
 
 // Prepare + search for nq device-resident queries on one device.
-dvs_status search_on(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L, dvs_mode mode,
-                     uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st, bool timed,
-                     bool out_slots) {
+dvs_status search_on(dvs_index* ix, Device& d, Scratch& sc, const float* d_q, uint32_t nq, uint32_t k, uint32_t L,
+                     dvs_mode mode, uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st,
+                     bool timed, bool out_slots) {
   if (d.lay.R > 64) return fail(DVS_ERR_UNSUPPORTED, "max out-degree above 64 is not supported by the search kernel");
-  // after the previous search on this device, whichever stream it used
-  DVS_CUDA(cudaStreamWaitEvent(st, d.done, 0));
-  dvs_status rc = search_enqueue(ix, d, d_q, nq, k, L, mode, d_ids, d_dist, d_counters, st, timed, out_slots);
-  const cudaError_t e = cudaEventRecord(d.done, st);
+  // after the previous search on this scratch, whichever stream it used
+  DVS_CUDA(cudaStreamWaitEvent(st, sc.done, 0));
+  dvs_status rc = search_enqueue(ix, d, sc, d_q, nq, k, L, mode, d_ids, d_dist, d_counters, st, timed, out_slots);
+  const cudaError_t e = cudaEventRecord(sc.done, st);
   if (rc == DVS_OK && e != cudaSuccess)
     return fail(DVS_ERR_CUDA, std::string("cudaEventRecord: ") + cudaGetErrorString(e));
   return rc;
 }
 
-dvs_status search_enqueue(dvs_index* ix, Device& d, const float* d_q, uint32_t nq, uint32_t k, uint32_t L,
-                          dvs_mode mode, uint32_t* d_ids, float* d_dist, uint32_t* d_counters, cudaStream_t st,
-                          bool timed, bool out_slots) {
+dvs_status search_enqueue(dvs_index* ix, Device& d, Scratch& sc, const float* d_q, uint32_t nq, uint32_t k,
+                          uint32_t L, dvs_mode mode, uint32_t* d_ids, float* d_dist, uint32_t* d_counters,
+                          cudaStream_t st, bool timed, bool out_slots) {
   const DevLayout& lay = d.lay;
   const bool rabitq = mode == DVS_MODE_RABITQ_GPU;
   if (lay.n == 0) {
     // an index created empty and not yet inserted into: every result slot is empty
-    if (timed) DVS_CUDA(cudaEventRecord(d.ev0, st));
+    if (timed) DVS_CUDA(cudaEventRecord(sc.ev0, st));
     DVS_CUDA(cudaMemsetAsync(d_ids, 0xFF, size_t(nq) * k * 4, st));
     DVS_CUDA(launch_fill_f32(d_dist, size_t(nq) * k, __builtin_huge_valf(), st));
     if (d_counters) DVS_CUDA(cudaMemsetAsync(d_counters, 0, size_t(nq) * 16, st));
-    DVS_CUDA(cudaMemsetAsync(d.work, 0, 16, st));
-    if (timed) DVS_CUDA(cudaEventRecord(d.ev1, st));
+    DVS_CUDA(cudaMemsetAsync(sc.work, 0, 16, st));
+    if (timed) DVS_CUDA(cudaEventRecord(sc.ev1, st));
     return DVS_OK;
   }
   const uint32_t cap = rabitq ? L + kBeamSlack : L;
   LaunchShape s;
   dvs_status rc = launch_shape(d, cap, ix->slots_per_entry, !rabitq, s);
   if (rc != DVS_OK) return rc;
-  rc = ensure_scratch(d, nq, k, false);
+  rc = ensure_scratch(d, sc, nq, k, false);
   if (rc != DVS_OK) return rc;
   const uint32_t blocks_full = s.blocks_per_sm * d.sm_count;
-  const uint32_t blocks_needed = (nq + s.qpb - 1) / s.qpb;
+  const uint32_t blocks_needed = (nq + s.wpb - 1) / s.wpb;
   const uint32_t blocks = std::max(1u, std::min(blocks_full, blocks_needed));
-  const size_t slots = size_t(blocks) * s.qpb;
-  if (slots > d.ovf_slots) {
+  const size_t slots = size_t(blocks) * s.wpb;
+  if (slots > sc.ovf_slots) {
     // spill tables and their epoch words start zeroed: every entry empty
-    dev_free(d.ovf);
-    DVS_CUDA(cudaMalloc(&d.ovf, slots * (size_t(kOverflowSlots) + 1) * 4));
-    DVS_CUDA(cudaMemsetAsync(d.ovf, 0, slots * (size_t(kOverflowSlots) + 1) * 4, st));
-    d.ovf_slots = slots;
+    dev_free(sc.ovf);
+    DVS_CUDA(cudaMalloc(&sc.ovf, slots * (size_t(kOverflowSlots) + 1) * 4));
+    DVS_CUDA(cudaMemsetAsync(sc.ovf, 0, slots * (size_t(kOverflowSlots) + 1) * 4, st));
+    sc.ovf_slots = slots;
   }
-  DVS_CUDA(cudaMemsetAsync(d.work, 0, 16, st));
+  DVS_CUDA(cudaMemsetAsync(sc.work, 0, 16, st));
   cudaEvent_t* tr = nullptr;
-  if (ix->kernel_timing && !d.tev.empty()) {
+  if (ix->kernel_timing && &sc == &d.sc && !d.tev.empty()) {
     if (d.tcount < Device::kRing) tr = &d.tev[3 * d.tcount++];
   }
-  if (timed) DVS_CUDA(cudaEventRecord(d.ev0, st));
+  if (timed) DVS_CUDA(cudaEventRecord(sc.ev0, st));
   if (tr) DVS_CUDA(cudaEventRecord(tr[0], st));
   if (rabitq) {
     if (ix->rotation == DVS_ROTATION_TENSOR)
-      DVS_CUDA(launch_prepare_tc(d_q, lay.dim, d.tc, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits,
-                                 nq, d.work + 1, st));
+      DVS_CUDA(launch_prepare_tc(d_q, lay.dim, d.tc, lay.c_rot, sc.qrot, lay.vec_stride, sc.qfac, 4, lay.dim, lay.bits,
+                                 nq, sc.work + 1, st));
     else
-      DVS_CUDA(launch_prepare(d_q, lay.dim, lay.P, lay.c_rot, d.qrot, lay.vec_stride, d.qfac, 4, lay.dim, lay.bits, nq,
+      DVS_CUDA(launch_prepare(d_q, lay.dim, lay.P, lay.c_rot, sc.qrot, lay.vec_stride, sc.qfac, 4, lay.dim, lay.bits, nq,
                               st));
   }
   if (tr) DVS_CUDA(cudaEventRecord(tr[1], st));
   SearchArgs a;
   a.ix = lay;
   a.queries = d_q;
-  a.qrot = d.qrot;
-  a.qfac = d.qfac;
+  a.qrot = sc.qrot;
+  a.qfac = sc.qfac;
   a.nq = nq;
   a.k = k;
   a.L = L;
@@ -300,10 +292,10 @@ dvs_status search_enqueue(dvs_index* ix, Device& d, const float* d_q, uint32_t n
   a.hop_limit = ix->hop_limit;
   a.out_ids = d_ids;
   a.out_dist = d_dist;
-  a.counters = d_counters ? d_counters : d.counters;
-  a.work = d.work;
-  a.ovf = d.ovf;
-  a.ovf_epoch = d.ovf + d.ovf_slots * kOverflowSlots;
+  a.counters = d_counters ? d_counters : sc.counters;
+  a.work = sc.work;
+  a.ovf = sc.ovf;
+  a.ovf_epoch = sc.ovf + sc.ovf_slots * kOverflowSlots;
   a.ovf_cap = kOverflowSlots;
   a.ovf_limit = kOverflowSlots / 10 * 8;
   a.ovf_tagged = lay.n < (uint64_t(1) << 24) ? 1u : 0u;
@@ -317,7 +309,7 @@ dvs_status search_enqueue(dvs_index* ix, Device& d, const float* d_q, uint32_t n
   a.out_slots = out_slots ? 1u : 0u;
   DVS_CUDA(launch_search(a, s.wpb, blocks, st));
   if (tr) DVS_CUDA(cudaEventRecord(tr[2], st));
-  if (timed) DVS_CUDA(cudaEventRecord(d.ev1, st));
+  if (timed) DVS_CUDA(cudaEventRecord(sc.ev1, st));
   return DVS_OK;
 }
 
@@ -455,8 +447,6 @@ dvs_status dvs_create(const dvs_create_params* p, dvs_index** out) {
 dvs_status dvs_close(dvs_index* ix) {
   if (!ix) return fail(DVS_ERR_ARG, "null index");
   for (auto& d : ix->devs) {
-    cudaSetDevice(d.ordinal);
-    if (d.stream) cudaStreamSynchronize(d.stream);
     d.release();
   }
   delete ix;
@@ -501,9 +491,9 @@ dvs_status dvs_set_rotation(dvs_index* ix, dvs_rotation rotation) {
     for (auto& d : ix->devs) {
       if (d.tc.split) continue;
       DVS_CUDA(cudaSetDevice(d.ordinal));
-      DVS_CUDA(cudaStreamSynchronize(d.stream));
-      DVS_CUDA(dvs::tc_rotation_prepare(d.P, d.lay.dim, &d.tc, d.stream));
-      DVS_CUDA(cudaStreamSynchronize(d.stream));
+      DVS_CUDA(cudaStreamSynchronize(d.sc.stream));
+      DVS_CUDA(dvs::tc_rotation_prepare(d.P, d.lay.dim, &d.tc, d.sc.stream));
+      DVS_CUDA(cudaStreamSynchronize(d.sc.stream));
     }
   }
   ix->rotation = rotation;
@@ -594,8 +584,8 @@ dvs_status dvs_search_device(dvs_index* ix, uint32_t slot, const float* d_querie
   std::lock_guard<std::mutex> g(ix->mu);
   dvs::Device& d = ix->devs[slot];
   DVS_CUDA(cudaSetDevice(d.ordinal));
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : d.stream;
-  return dvs::search_on(ix, d, d_queries, nq, k, L, mode, d_out_ids, d_out_dist, d_counters, st, false);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : d.sc.stream;
+  return dvs::search_on(ix, d, d.sc, d_queries, nq, k, L, mode, d_out_ids, d_out_dist, d_counters, st, false);
 }
 
 dvs_status dvs_search(dvs_index* ix, const float* h_queries, uint32_t nq, uint32_t dim, uint32_t k, uint32_t L,
@@ -615,23 +605,24 @@ dvs_status dvs_search(dvs_index* ix, const float* h_queries, uint32_t nq, uint32
     const size_t q0 = nq * i / nd, q1 = nq * (i + 1) / nd, m = q1 - q0;
     if (m == 0) return;
     auto body = [&]() -> dvs_status {
+      dvs::Scratch& sc = d.sc;
       DVS_CUDA(cudaSetDevice(d.ordinal));
-      dvs_status r = dvs::ensure_scratch(d, m, k, true);
+      dvs_status r = dvs::ensure_scratch(d, sc, m, k, true);
       if (r != DVS_OK) return r;
-      DVS_CUDA(cudaMemcpyAsync(d.queries, h_queries + q0 * dim, m * dim * 4, cudaMemcpyHostToDevice, d.stream));
-      r = dvs::search_on(ix, d, d.queries, uint32_t(m), k, L, mode, d.out_ids, d.out_dist, d.counters, d.stream, true);
+      DVS_CUDA(cudaMemcpyAsync(sc.queries, h_queries + q0 * dim, m * dim * 4, cudaMemcpyHostToDevice, sc.stream));
+      r = dvs::search_on(ix, d, sc, sc.queries, uint32_t(m), k, L, mode, sc.out_ids, sc.out_dist, sc.counters, sc.stream, true);
       if (r != DVS_OK) return r;
-      DVS_CUDA(cudaMemcpyAsync(h_out_ids + q0 * k, d.out_ids, m * k * 4, cudaMemcpyDeviceToHost, d.stream));
-      DVS_CUDA(cudaMemcpyAsync(h_out_dist + q0 * k, d.out_dist, m * k * 4, cudaMemcpyDeviceToHost, d.stream));
+      DVS_CUDA(cudaMemcpyAsync(h_out_ids + q0 * k, sc.out_ids, m * k * 4, cudaMemcpyDeviceToHost, sc.stream));
+      DVS_CUDA(cudaMemcpyAsync(h_out_dist + q0 * k, sc.out_dist, m * k * 4, cudaMemcpyDeviceToHost, sc.stream));
       // per-query counters come back only when the caller asked for statistics
       std::vector<uint32_t> cnt(stats ? m * 4 : 0);
       uint32_t work[4] = {0, 0, 0, 0};
-      if (stats) DVS_CUDA(cudaMemcpyAsync(cnt.data(), d.counters, m * 16, cudaMemcpyDeviceToHost, d.stream));
-      DVS_CUDA(cudaMemcpyAsync(work, d.work, 16, cudaMemcpyDeviceToHost, d.stream));
-      DVS_CUDA(cudaStreamSynchronize(d.stream));
+      if (stats) DVS_CUDA(cudaMemcpyAsync(cnt.data(), sc.counters, m * 16, cudaMemcpyDeviceToHost, sc.stream));
+      DVS_CUDA(cudaMemcpyAsync(work, sc.work, 16, cudaMemcpyDeviceToHost, sc.stream));
+      DVS_CUDA(cudaStreamSynchronize(sc.stream));
       if (stats) {
         float ms = 0.f;
-        DVS_CUDA(cudaEventElapsedTime(&ms, d.ev0, d.ev1));
+        DVS_CUDA(cudaEventElapsedTime(&ms, sc.ev0, sc.ev1));
         dvs_stats& ps = part[i];
         for (size_t q = 0; q < m; ++q) {
           ps.expansions += cnt[q * 4 + 0];

@@ -80,16 +80,44 @@ __device__ __forceinline__ float l2_quad_partial(const float* __restrict__ q, co
   return acc;
 }
 
+// L2 cache policies (createpolicy): lines read under `keep` are evicted after
+// other lines, lines read under `stream` first.
+__device__ __forceinline__ uint64_t l2_policy_keep() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_stream() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// A read-only 16-byte load under an L2 cache policy.
+__device__ __forceinline__ uint4 ldg_hint(const uint4* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ float4 ldg_hint(const float4* p, uint64_t pol) {
+  const uint4 v = ldg_hint(reinterpret_cast<const uint4*>(p), pol);
+  return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
+}
+
 // l2_quad_partial of two rows at once (xB may equal xA): the same chain per
 // row, the two chains interleaved so their loads and FMAs overlap, each q
-// chunk read once for both.
+// chunk read once for both.  HINT: the rows are read under L2 policy `pol`.
+template <bool HINT = false>
 __device__ __forceinline__ void l2_quad_partial2(const float* __restrict__ q, const float* __restrict__ xA,
                                                  const float* __restrict__ xB, uint32_t dim, uint32_t t, float& accA,
-                                                 float& accB) {
+                                                 float& accB, uint64_t pol = 0) {
   const uint32_t n4 = dim >> 2;
   const float4* q4 = reinterpret_cast<const float4*>(q);
   const float4* a4 = reinterpret_cast<const float4*>(xA);
   const float4* b4 = reinterpret_cast<const float4*>(xB);
+  auto ld = [pol](const float4* p) { return HINT ? ldg_hint(p, pol) : __ldg(p); };
   float sa = 0.f, sb = 0.f;
 #define DVS_ACC4_2(Q, A, B)                                              \
   {                                                                      \
@@ -109,8 +137,8 @@ __device__ __forceinline__ void l2_quad_partial2(const float* __restrict__ q, co
     float4 a[4], b[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      a[k] = __ldg(a4 + i + 4 * k);
-      b[k] = __ldg(b4 + i + 4 * k);
+      a[k] = ld(a4 + i + 4 * k);
+      b[k] = ld(b4 + i + 4 * k);
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -119,7 +147,7 @@ __device__ __forceinline__ void l2_quad_partial2(const float* __restrict__ q, co
     }
   }
   for (; i < n4; i += 4) {
-    const float4 a = __ldg(a4 + i), b = __ldg(b4 + i);
+    const float4 a = ld(a4 + i), b = ld(b4 + i);
     const float4 c = q4[i];
     DVS_ACC4_2(c, a, b)
   }

@@ -795,9 +795,9 @@ dvs_status ensure_insert_scratch(Device& d, uint32_t m) {
   }
   uint32_t* k = d.ins_buf;
   size_t t1 = 0, t2 = 0, t3 = 0;
-  DVS_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, t1, k, k, k, k, int(m), 0, 32, d.stream));
-  DVS_CUDA(cub::DeviceRunLengthEncode::Encode(nullptr, t2, k, k, k, k, int(m), d.stream));
-  DVS_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, t3, k, k, int(m) + 1, d.stream));
+  DVS_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, t1, k, k, k, k, int(m), 0, 32, d.ins.stream));
+  DVS_CUDA(cub::DeviceRunLengthEncode::Encode(nullptr, t2, k, k, k, k, int(m), d.ins.stream));
+  DVS_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, t3, k, k, int(m) + 1, d.ins.stream));
   const size_t temp = std::max({t1, t2, t3});
   if (temp > d.ins_temp_bytes) {
     dev_free(d.ins_temp);
@@ -809,14 +809,14 @@ dvs_status ensure_insert_scratch(Device& d, uint32_t m) {
   return DVS_OK;
 }
 
-// Quantizes rows already rotated in d.qrot (b of them) into records row0..row0+b-1.
+// Quantizes rows already rotated in d.ins.qrot (b of them) into records row0..row0+b-1.
 dvs_status quantize_rows(Device& d, uint32_t b, uint64_t row0, double tc) {
   const DevLayout& L = d.lay;
   const uint32_t blocks = (b + kQuantPerBlock - 1) / kQuantPerBlock;
   const size_t smem = size_t(kQuantPerBlock) * L.dim;
   if (smem > 48 * 1024)
     DVS_CUDA(cudaFuncSetAttribute(insert_quantize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  insert_quantize_kernel<<<blocks, 32, smem, d.stream>>>(d.qrot, L.vec_stride, L.c_rot, 0.0 + tc, L.dim, L.bits, b,
+  insert_quantize_kernel<<<blocks, 32, smem, d.ins.stream>>>(d.ins.qrot, L.vec_stride, L.c_rot, 0.0 + tc, L.dim, L.bits, b,
                                                          d.rec, L.rec_words, L.code_words, row0);
   DVS_CUDA(cudaGetLastError());
   return DVS_OK;
@@ -825,41 +825,44 @@ dvs_status quantize_rows(Device& d, uint32_t b, uint64_t row0, double tc) {
 // One step of b vectors on one device (all b search the graph of the step's start).
 dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t* hid, uint32_t b, uint32_t Lc,
                        float alpha, dvs_insert_stats& st) {
-  DevLayout& L = d.lay;
+  // only inserts change the layout and they run one at a time: a copy needs
+  // no lock; what the step changes is published under the index lock
+  DevLayout L = d.lay;
   const uint32_t dim = L.dim, R = L.R;
   const double tc = ix->host.info.t_const;
   const uint64_t n0 = L.n;
-  dvs_status r = ensure_scratch(d, b, Lc, true);
+  dvs_status r = ensure_scratch(d, d.ins, b, Lc, true);
   if (r == DVS_OK) r = ensure_insert_scratch(d, b * R);
   if (r != DVS_OK) return r;
-  DVS_CUDA(cudaMemcpyAsync(d.queries, hx, size_t(b) * dim * 4, cudaMemcpyHostToDevice, d.stream));
+  DVS_CUDA(cudaMemcpyAsync(d.ins.queries, hx, size_t(b) * dim * 4, cudaMemcpyHostToDevice, d.ins.stream));
   // the vectors, ids and records of the new rows
-  DVS_CUDA(cudaMemcpy2DAsync(d.vecs + n0 * L.vec_stride, size_t(L.vec_stride) * 4, d.queries, size_t(dim) * 4,
-                             size_t(dim) * 4, b, cudaMemcpyDeviceToDevice, d.stream));
-  DVS_CUDA(cudaMemcpyAsync(d.ids + n0, hid, size_t(b) * 4, cudaMemcpyHostToDevice, d.stream));
-  DVS_CUDA(launch_prepare(d.queries, dim, L.P, L.c_rot, d.qrot, L.vec_stride, d.qfac, 4, dim, L.bits, b, d.stream));
+  DVS_CUDA(cudaMemcpy2DAsync(d.vecs + n0 * L.vec_stride, size_t(L.vec_stride) * 4, d.ins.queries, size_t(dim) * 4,
+                             size_t(dim) * 4, b, cudaMemcpyDeviceToDevice, d.ins.stream));
+  DVS_CUDA(cudaMemcpyAsync(d.ids + n0, hid, size_t(b) * 4, cudaMemcpyHostToDevice, d.ins.stream));
+  DVS_CUDA(launch_prepare(d.ins.queries, dim, L.P, L.c_rot, d.ins.qrot, L.vec_stride, d.ins.qfac, 4, dim, L.bits, b, d.ins.stream));
   r = quantize_rows(d, b, n0, tc);
   if (r != DVS_OK) return r;
   if (n0 == 0) {
     // first node of an empty index: the medoid, no neighbours
-    DVS_CUDA(cudaMemsetAsync(d.adj, 0xFF, size_t(R) * 4, d.stream));
-    DVS_CUDA(cudaStreamSynchronize(d.stream));
-    L.medoid = 0;
-    L.n = 1;
+    DVS_CUDA(cudaMemsetAsync(d.adj, 0xFF, size_t(R) * 4, d.ins.stream));
+    DVS_CUDA(cudaStreamSynchronize(d.ins.stream));
+    std::lock_guard<std::mutex> g(ix->mu);
+    d.lay.medoid = 0;
+    d.lay.n = 1;
     d.rows = 1;
     return DVS_OK;
   }
   // 1. beam search with exact distances, capacity L_c; the whole final beam as slots
-  r = search_on(ix, d, d.queries, b, Lc, Lc, DVS_MODE_EXACT_GPU, d.out_ids, d.out_dist, d.counters, d.stream, true,
+  r = search_on(ix, d, d.ins, d.ins.queries, b, Lc, Lc, DVS_MODE_EXACT_GPU, d.ins.out_ids, d.ins.out_dist, d.ins.counters, d.ins.stream, true,
                 true);
   if (r != DVS_OK) return r;
   // 3. RobustPrune of each beam into the new adjacency rows
-  DVS_CUDA(cudaEventRecord(d.ins_ev[0], d.stream));
+  DVS_CUDA(cudaEventRecord(d.ins_ev[0], d.ins.stream));
   const size_t pstaged = size_t(Lc) * prune_row_stride4(L.vec_stride) * 16 + size_t(Lc) * 9 + 16;
   if (pstaged <= kStageBudget) {
     if (pstaged > 48 * 1024)
       DVS_CUDA(cudaFuncSetAttribute(insert_prune_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(pstaged)));
-    insert_prune_kernel<<<b, kPruneThreads, pstaged, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha, n0,
+    insert_prune_kernel<<<b, kPruneThreads, pstaged, d.ins.stream>>>(L, d.ins.out_ids, d.ins.out_dist, d.ins.counters, Lc, alpha, n0,
                                                                  d.adj);
   } else {
     const size_t psmem = prune_passes_bytes(Lc, L.vec_stride);
@@ -867,12 +870,12 @@ dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t
     if (psmem > 48 * 1024)
       DVS_CUDA(cudaFuncSetAttribute(insert_prune_passes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(psmem)));
-    insert_prune_passes_kernel<<<b, kPruneThreads, psmem, d.stream>>>(L, d.out_ids, d.out_dist, d.counters, Lc, alpha,
+    insert_prune_passes_kernel<<<b, kPruneThreads, psmem, d.ins.stream>>>(L, d.ins.out_ids, d.ins.out_dist, d.ins.counters, Lc, alpha,
                                                                       n0, d.adj);
   }
   DVS_CUDA(cudaGetLastError());
-  DVS_CUDA(cudaEventRecord(d.ins_ev[1], d.stream));
-  sum_counters_kernel<<<std::min<uint32_t>((b + 255) / 256, 64), 256, 0, d.stream>>>(d.counters, b, d.ins_stats);
+  DVS_CUDA(cudaEventRecord(d.ins_ev[1], d.ins.stream));
+  sum_counters_kernel<<<std::min<uint32_t>((b + 255) / 256, 64), 256, 0, d.ins.stream>>>(d.ins.counters, b, d.ins_stats);
   DVS_CUDA(cudaGetLastError());
   // 5. reverse edges: (target, new slot) pairs grouped by target on the device
   //    with a stable radix sort (insert order kept inside a group)
@@ -885,16 +888,16 @@ dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t
   uint32_t* run_cnt = run_tg + m;        // m + 1 entries
   uint32_t* run_off = run_cnt + m + 1;   // m + 1 entries
   uint32_t* nruns = run_off + m + 1;
-  DVS_CUDA(cudaEventRecord(d.ins_ev[2], d.stream));
-  edge_pairs_kernel<<<(m + 255) / 256, 256, 0, d.stream>>>(d.adj + n0 * R, m, R, uint32_t(n0), keys_in, vals_in);
+  DVS_CUDA(cudaEventRecord(d.ins_ev[2], d.ins.stream));
+  edge_pairs_kernel<<<(m + 255) / 256, 256, 0, d.ins.stream>>>(d.adj + n0 * R, m, R, uint32_t(n0), keys_in, vals_in);
   DVS_CUDA(cudaGetLastError());
   size_t tb = d.ins_temp_bytes;
   DVS_CUDA(cub::DeviceRadixSort::SortPairs(d.ins_temp, tb, keys_in, keys_out, vals_in, vals_out, int(m), 0, 32,
-                                           d.stream));
+                                           d.ins.stream));
   tb = d.ins_temp_bytes;
-  DVS_CUDA(cub::DeviceRunLengthEncode::Encode(d.ins_temp, tb, keys_out, run_tg, run_cnt, nruns, int(m), d.stream));
+  DVS_CUDA(cub::DeviceRunLengthEncode::Encode(d.ins_temp, tb, keys_out, run_tg, run_cnt, nruns, int(m), d.ins.stream));
   tb = d.ins_temp_bytes;
-  DVS_CUDA(cub::DeviceScan::ExclusiveSum(d.ins_temp, tb, run_cnt, run_off, int(m) + 1, d.stream));
+  DVS_CUDA(cub::DeviceScan::ExclusiveSum(d.ins_temp, tb, run_cnt, run_off, int(m) + 1, d.ins.stream));
   L.n = n0 + b;
   if (rev_warp_bytes(R, L.vec_stride, true) > kRevStageMax && rev_block_bytes(R, L.vec_stride) <= 227 * 1024) {
     // wide rows: a block per target shares one staging
@@ -905,7 +908,7 @@ dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t
     DVS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, reverse_edges_block_kernel, kRevThreads, smem));
     if (bps == 0) return fail(DVS_ERR_CAPACITY, "reverse-edge block needs more shared memory than a block has");
     const uint32_t blocks = std::max(1u, std::min<uint32_t>(m, d.sm_count * uint32_t(bps)));
-    reverse_edges_block_kernel<<<blocks, kRevThreads, smem, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
+    reverse_edges_block_kernel<<<blocks, kRevThreads, smem, d.ins.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
                                                                         alpha, d.ins_stats);
   } else {
     // staged when a warp's candidate rows fit kRevStageMax; warps per block
@@ -939,23 +942,27 @@ dvs_status insert_step(dvs_index* ix, Device& d, const float* hx, const uint32_t
     if (staged) {
       DVS_CUDA(cudaFuncSetAttribute(reverse_edges_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(smem)));
-      reverse_edges_kernel<true><<<blocks, wpb * 32, smem, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
+      reverse_edges_kernel<true><<<blocks, wpb * 32, smem, d.ins.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
                                                                        alpha, d.ins_stats);
     } else {
       DVS_CUDA(cudaFuncSetAttribute(reverse_edges_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     int(smem)));
-      reverse_edges_kernel<false><<<blocks, wpb * 32, smem, d.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
+      reverse_edges_kernel<false><<<blocks, wpb * 32, smem, d.ins.stream>>>(L, d.adj, run_tg, run_off, vals_out, nruns,
                                                                         alpha, d.ins_stats);
     }
   }
   DVS_CUDA(cudaGetLastError());
-  DVS_CUDA(cudaEventRecord(d.ins_ev[3], d.stream));
+  DVS_CUDA(cudaEventRecord(d.ins_ev[3], d.ins.stream));
   uint32_t work[4] = {0, 0, 0, 0};
-  DVS_CUDA(cudaMemcpyAsync(work, d.work, 16, cudaMemcpyDeviceToHost, d.stream));
-  DVS_CUDA(cudaStreamSynchronize(d.stream));
-  d.rows = L.n;
+  DVS_CUDA(cudaMemcpyAsync(work, d.ins.work, 16, cudaMemcpyDeviceToHost, d.ins.stream));
+  DVS_CUDA(cudaStreamSynchronize(d.ins.stream));
+  {
+    std::lock_guard<std::mutex> g(ix->mu);
+    d.lay.n = L.n;
+    d.rows = L.n;
+  }
   float ms = 0.f;
-  DVS_CUDA(cudaEventElapsedTime(&ms, d.ev0, d.ev1));
+  DVS_CUDA(cudaEventElapsedTime(&ms, d.ins.ev0, d.ins.ev1));
   st.device_ms += ms;
   DVS_CUDA(cudaEventElapsedTime(&ms, d.ins_ev[0], d.ins_ev[1]));
   st.prune_ms += ms;
@@ -975,24 +982,25 @@ dvs_status grow_rows(Device& d, uint64_t rows) {
   const uint64_t cap = std::max<uint64_t>({rows, d.cap_rows * 2, 1024});
   const uint64_t n = L.n;
   DVS_CUDA(cudaSetDevice(d.ordinal));
-  DVS_CUDA(cudaStreamSynchronize(d.stream));
+  DVS_CUDA(cudaStreamSynchronize(d.ins.stream));
+  DVS_CUDA(cudaStreamSynchronize(d.sc.stream));
   uint32_t *adj = nullptr, *rec = nullptr, *ids = nullptr;
   float* vecs = nullptr;
   DVS_CUDA(cudaMalloc(&adj, cap * L.R * 4));
   DVS_CUDA(cudaMalloc(&rec, cap * L.rec_words * 4));
   DVS_CUDA(cudaMalloc(&vecs, cap * L.vec_stride * 4));
   DVS_CUDA(cudaMalloc(&ids, cap * 4));
-  DVS_CUDA(cudaMemsetAsync(adj, 0xFF, cap * L.R * 4, d.stream));
-  DVS_CUDA(cudaMemsetAsync(rec, 0, cap * L.rec_words * 4, d.stream));
-  DVS_CUDA(cudaMemsetAsync(vecs, 0, cap * L.vec_stride * 4, d.stream));
-  DVS_CUDA(cudaMemsetAsync(ids, 0, cap * 4, d.stream));
+  DVS_CUDA(cudaMemsetAsync(adj, 0xFF, cap * L.R * 4, d.sc.stream));
+  DVS_CUDA(cudaMemsetAsync(rec, 0, cap * L.rec_words * 4, d.sc.stream));
+  DVS_CUDA(cudaMemsetAsync(vecs, 0, cap * L.vec_stride * 4, d.sc.stream));
+  DVS_CUDA(cudaMemsetAsync(ids, 0, cap * 4, d.sc.stream));
   if (n) {
-    DVS_CUDA(cudaMemcpyAsync(adj, d.adj, n * L.R * 4, cudaMemcpyDeviceToDevice, d.stream));
-    DVS_CUDA(cudaMemcpyAsync(rec, d.rec, n * L.rec_words * 4, cudaMemcpyDeviceToDevice, d.stream));
-    DVS_CUDA(cudaMemcpyAsync(vecs, d.vecs, n * L.vec_stride * 4, cudaMemcpyDeviceToDevice, d.stream));
-    DVS_CUDA(cudaMemcpyAsync(ids, d.ids, n * 4, cudaMemcpyDeviceToDevice, d.stream));
+    DVS_CUDA(cudaMemcpyAsync(adj, d.adj, n * L.R * 4, cudaMemcpyDeviceToDevice, d.sc.stream));
+    DVS_CUDA(cudaMemcpyAsync(rec, d.rec, n * L.rec_words * 4, cudaMemcpyDeviceToDevice, d.sc.stream));
+    DVS_CUDA(cudaMemcpyAsync(vecs, d.vecs, n * L.vec_stride * 4, cudaMemcpyDeviceToDevice, d.sc.stream));
+    DVS_CUDA(cudaMemcpyAsync(ids, d.ids, n * 4, cudaMemcpyDeviceToDevice, d.sc.stream));
   }
-  DVS_CUDA(cudaStreamSynchronize(d.stream));
+  DVS_CUDA(cudaStreamSynchronize(d.sc.stream));
   dev_free(d.adj);
   dev_free(d.rec);
   dev_free(d.vecs);
@@ -1015,9 +1023,12 @@ extern "C" {
 
 dvs_status dvs_reserve(dvs_index* ix, uint64_t capacity) {
   if (!ix) return fail(DVS_ERR_ARG, "null index");
+  std::lock_guard<std::mutex> gi(ix->ins_mu);
   std::lock_guard<std::mutex> g(ix->mu);
   for (auto& d : ix->devs) {
     if (d.lay.shard_log != 0) return fail(DVS_ERR_UNSUPPORTED, "online insert needs a replicated index");
+    DVS_CUDA(cudaSetDevice(d.ordinal));
+    DVS_CUDA(cudaDeviceSynchronize());  // searches in flight on any stream finish first
     const dvs_status s = dvs::grow_rows(d, capacity);
     if (s != DVS_OK) return s;
   }
@@ -1040,21 +1051,33 @@ dvs_status dvs_insert(dvs_index* ix, const float* h_vectors, const uint32_t* h_i
   const uint32_t max_batch = p && p->max_batch ? p->max_batch : dvs::kInsertDefaultBatch;
   if (Lc > 4096) return fail(DVS_ERR_ARG, "beam_width_construction above 4096 is not supported");
   if (ix->host.info.R > 64) return fail(DVS_ERR_UNSUPPORTED, "max out-degree above 64 is not supported");
-  std::lock_guard<std::mutex> g(ix->mu);
-  for (auto& d : ix->devs)
-    if (d.lay.shard_log != 0) return fail(DVS_ERR_UNSUPPORTED, "online insert needs a replicated index");
-  const uint64_t n_start = ix->devs[0].lay.n;
-  if (n_start + n > 0xFFFFFFFEull) return fail(DVS_ERR_CAPACITY, "an index holds at most 2^32 - 2 nodes");
+  // one insert at a time; searches hold the index lock only to enqueue, and
+  // an insert takes it to grow the arrays and to publish each step, so
+  // searches run on the GPU while an insert step does
+  std::lock_guard<std::mutex> gi(ix->ins_mu);
+  uint64_t n_start = 0;
+  {
+    std::lock_guard<std::mutex> g(ix->mu);
+    for (auto& d : ix->devs)
+      if (d.lay.shard_log != 0) return fail(DVS_ERR_UNSUPPORTED, "online insert needs a replicated index");
+    n_start = ix->devs[0].lay.n;
+    if (n_start + n > 0xFFFFFFFEull) return fail(DVS_ERR_CAPACITY, "an index holds at most 2^32 - 2 nodes");
+    for (auto& d : ix->devs) {
+      if (n_start + n <= d.cap_rows) continue;
+      DVS_CUDA(cudaSetDevice(d.ordinal));
+      DVS_CUDA(cudaDeviceSynchronize());  // searches in flight on any stream finish before the arrays move
+      const dvs_status s = dvs::grow_rows(d, n_start + n);
+      if (s != DVS_OK) return s;
+    }
+  }
   std::vector<uint32_t> ids(n);
   for (uint32_t i = 0; i < n; ++i) ids[i] = h_ids ? h_ids[i] : uint32_t(n_start + i);
   dvs_insert_stats st{};
   for (auto& d : ix->devs) {
     DVS_CUDA(cudaSetDevice(d.ordinal));
-    DVS_CUDA(cudaDeviceSynchronize());  // searches in flight on any stream finish first
-    dvs_status s = dvs::grow_rows(d, n_start + n);
-    if (s != DVS_OK) return s;
+    dvs_status s = DVS_OK;
     if (!d.ins_stats) DVS_CUDA(cudaMalloc(&d.ins_stats, 4 * sizeof(unsigned long long)));
-    DVS_CUDA(cudaMemsetAsync(d.ins_stats, 0, 4 * sizeof(unsigned long long), d.stream));
+    DVS_CUDA(cudaMemsetAsync(d.ins_stats, 0, 4 * sizeof(unsigned long long), d.ins.stream));
     dvs_insert_stats dst{};
     uint32_t pos = 0;
     while (pos < n && s == DVS_OK) {
@@ -1067,8 +1090,8 @@ dvs_status dvs_insert(dvs_index* ix, const float* h_vectors, const uint32_t* h_i
     }
     if (s != DVS_OK) return s;
     unsigned long long cs[4] = {0, 0, 0, 0};
-    DVS_CUDA(cudaMemcpyAsync(cs, d.ins_stats, sizeof(cs), cudaMemcpyDeviceToHost, d.stream));
-    DVS_CUDA(cudaStreamSynchronize(d.stream));
+    DVS_CUDA(cudaMemcpyAsync(cs, d.ins_stats, sizeof(cs), cudaMemcpyDeviceToHost, d.ins.stream));
+    DVS_CUDA(cudaStreamSynchronize(d.ins.stream));
     dst.expansions = cs[0];
     dst.distances = cs[1];
     dst.full_prunes = cs[2];
@@ -1076,6 +1099,7 @@ dvs_status dvs_insert(dvs_index* ix, const float* h_vectors, const uint32_t* h_i
     dst.inserted = n;
     if (&d == &ix->devs[0]) st = dst;
   }
+  std::lock_guard<std::mutex> g(ix->mu);
   ix->host.info.num_vectors = ix->devs[0].lay.n;
   ix->host.info.medoid = ix->devs[0].lay.medoid;
   if (stats) *stats = st;

@@ -98,8 +98,8 @@ dvs_status noalloc_enqueue(dvs_index* ix, Device& d, const float* d_queries, uin
   float* qrot = reinterpret_cast<float*>(base + kWorkBytes + kEpochBytes + qfac_bytes);
   uint32_t* tables = reinterpret_cast<uint32_t*>(base + kTablesOffset);
   // one spill table per warp slot: as many blocks as have a table for every warp
-  const uint32_t blocks_needed = (nq + sh.qpb - 1) / sh.qpb;
-  const uint32_t blocks_fit = std::max(1u, kNoAllocTables / sh.qpb);
+  const uint32_t blocks_needed = (nq + sh.wpb - 1) / sh.wpb;
+  const uint32_t blocks_fit = std::max(1u, kNoAllocTables / sh.wpb);
   const uint32_t blocks = std::max(1u, std::min({sh.blocks_per_sm * d.sm_count, blocks_needed, blocks_fit}));
 
   DVS_CUDA(cudaMemsetAsync(work, 0, 16, st));
@@ -172,12 +172,12 @@ extern "C" dvs_status dvs_search_device_noalloc(dvs_index* index, uint32_t devic
                                       std::to_string(kNoAllocQueryBytes >> 20) +
                                       " MiB of its fixed scratch); got " + std::to_string(nq));
   DVS_CUDA(cudaSetDevice(d.ordinal));
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : d.stream;
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : d.sc.stream;
   // after the previous search on this device, whichever stream it used
-  DVS_CUDA(cudaStreamWaitEvent(st, d.done, 0));
+  DVS_CUDA(cudaStreamWaitEvent(st, d.sc.done, 0));
   const dvs_status rc = noalloc_enqueue(index, d, d_queries, nq, k, beam_width, mode == DVS_MODE_RABITQ_GPU,
                                         d_out_ids, d_out_dist, d_counters, st);
-  const cudaError_t e = cudaEventRecord(d.done, st);
+  const cudaError_t e = cudaEventRecord(d.sc.done, st);
   if (rc == DVS_OK && e != cudaSuccess)
     return fail(DVS_ERR_CUDA, std::string("cudaEventRecord: ") + cudaGetErrorString(e));
   return rc;

@@ -341,9 +341,10 @@ __device__ __forceinline__ void prefetch_record_l2(const DevLayout& ix, uint32_t
 // Exact L2 of `count` rows (slot ids in `rows`) against q, written to `out`;
 // 4 lanes per row, two rows per lane quad (rows i and i + 8), 16 rows per
 // round.  Warp-uniform control flow.
+template <bool HINT = false>
 __device__ __forceinline__ void l2_rows_warp(const DevLayout& ix, const float* __restrict__ q,
                                              const uint32_t* rows, uint32_t count, float* out, uint32_t lane,
-                                             uint32_t row_mask) {
+                                             uint32_t row_mask, uint64_t pol = 0) {
   const uint32_t t = lane & 3;
   for (uint32_t r0 = 0; r0 < count; r0 += 16) {
     const uint32_t iA = r0 + (lane >> 2), iB = iA + 8;
@@ -351,7 +352,7 @@ __device__ __forceinline__ void l2_rows_warp(const DevLayout& ix, const float* _
     if (iA < count) {
       const float* xA = vec_row(ix, rows[iA] & row_mask);
       const float* xB = iB < count ? vec_row(ix, rows[iB] & row_mask) : xA;
-      l2_quad_partial2(q, xA, xB, ix.dim, t, pA, pB);
+      l2_quad_partial2<HINT>(q, xA, xB, ix.dim, t, pA, pB, pol);
     }
     const float tA = quad_butterfly(pA), tB = quad_butterfly(pB);
     if (t == 0) {
@@ -453,150 +454,8 @@ constexpr int kWideRecs = 3, kWideBatch = 6;
 // loaded after the visited check (wider than 128 bytes): 168, three warps per
 // sub-partition.  The rest are bounded by shared memory or need their
 // registers, and keep up to 255.
-// Records wider than 128 bytes with 1/2/4-bit codes run cooperatively (a
-// query per CTA of 4 warps, estimates from shared memory): 128, four CTAs per
-// SM.
-__host__ __device__ constexpr bool search_coop(int bits, int rch, bool exact) { return rch == 0 && !exact && bits != 8; }
-
-__host__ __device__ constexpr int search_max_regs(int bits, int npl, int rch, bool exact) {
-  return search_coop(bits, rch, exact)         ? 128
-         : npl == 1 && (rch == 4 || exact)     ? 96
-         : npl == 1 && rch == 8                ? 128
-         : (rch == 0 && !exact)                ? 168
-                                               : 255;
-}
-
-// ---- cooperative wide-record search: a query per CTA of 4 warps ----
-// Warp 0 (the leader) runs the whole Vamana loop as a search warp does; the
-// other three warps join it only for the two wide phases, the estimates of an
-// expansion's fresh neighbours and the final rerank, through named barrier 1.
-// The records of every listed neighbour are fetched into a shared-memory
-// stage by one bulk copy each (this GPU's or a peer's memory, no multicast)
-// while the leader filters the visited set, so an expansion waits for one
-// memory round trip instead of a load batch per few chunks.
-constexpr uint32_t kCoopWarps = 4;
-constexpr uint32_t kCmdExit = 0, kCmdEstimate = 1, kCmdRerank = 2;
-constexpr uint32_t kCoopCtlWords = 8;  // cmd, count, q_add, q_k1, stage parity, pad; then the fresh list's row positions
-constexpr uint32_t kCoopWaitLimit = 1u << 22;
-
-__device__ __forceinline__ void coop_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ bool stage_wait(uint32_t mbar, uint32_t parity) {
-  for (uint32_t it = 0; it < kCoopWaitLimit; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(mbar), "r"(parity)
-        : "memory");
-    if (ok) return true;
-  }
-  return false;
-}
-
-// Chain t of two records' estimates (lane t of a lane quad, the reference
-// kernel's tile split: dims j = t mod 4 in ascending order), from records in
-// shared memory; the two chains run on packed two-lane FMAs sharing each q'
-// value.  `q` is this lane's chain of the chain-major q'.
-template <int BITS>
-__device__ __forceinline__ float2 estimate_pair_smem(const uint32_t* rA, const uint32_t* rB, uint32_t dim,
-                                                     const float* __restrict__ q, uint32_t t) {
-  constexpr uint32_t kPer = 32 / BITS, kMask = (1u << BITS) - 1u;
-  const float2 nm = make_float2(-8388608.0f, -8388608.0f);
-  const uint32_t nch = (dim / kPer) >> 2;  // chunks whose every dim is < dim
-  const uint32_t sh0 = BITS * t;
-  float2 s = make_float2(0.f, 0.f);
-  for (uint32_t ch = 0; ch < nch; ++ch) {
-    const uint4 va = reinterpret_cast<const uint4*>(rA)[ch];
-    const uint4 vb = reinterpret_cast<const uint4*>(rB)[ch];
-    float qf[kPer];
-    const float4* q4 = reinterpret_cast<const float4*>(q + ch * kPer);
-#pragma unroll
-    for (uint32_t g = 0; g < kPer / 4; ++g) {
-      const float4 f = q4[g];
-      qf[4 * g] = f.x;
-      qf[4 * g + 1] = f.y;
-      qf[4 * g + 2] = f.z;
-      qf[4 * g + 3] = f.w;
-    }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const uint32_t wa = e == 0 ? va.x : e == 1 ? va.y : e == 2 ? va.z : va.w;
-      const uint32_t wb = e == 0 ? vb.x : e == 1 ? vb.y : e == 2 ? vb.z : vb.w;
-#pragma unroll
-      for (uint32_t i = 0; i < kPer / 4; ++i) {
-        const uint32_t sh = sh0 + 4 * BITS * i;
-        const float qv = qf[e * (kPer / 4) + i];
-        const float2 c = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | ((wa >> sh) & kMask)),
-                                                __uint_as_float(0x4B000000u | ((wb >> sh) & kMask))),
-                                    nm);
-        s = __ffma2_rn(c, make_float2(qv, qv), s);
-      }
-    }
-  }
-  // words past the last whole chunk, the partial last word included
-  for (uint32_t wi = nch * 4; wi * kPer < dim; ++wi) {
-    const uint32_t wa = rA[wi], wb = rB[wi], j0 = wi * kPer;
-    for (uint32_t n = t; n < kPer && j0 + n < dim; n += 4) {
-      const float qv = q[(j0 + n) >> 2];
-      const float2 c = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | ((wa >> (BITS * n)) & kMask)),
-                                              __uint_as_float(0x4B000000u | ((wb >> (BITS * n)) & kMask))),
-                                  nm);
-      s = __ffma2_rn(c, make_float2(qv, qv), s);
-    }
-  }
-  return s;
-}
-
-// This warp's share of the estimates of the m fresh neighbours (m <= 64):
-// lane quad g = warp * 8 + lane / 4 of the CTA takes candidates g and g + 32,
-// whose records sit in the stage at their adjacency-row positions.
-template <int BITS>
-__device__ __forceinline__ void coop_estimate(const DevLayout& ix, const uint32_t* stage, const uint32_t* cpos,
-                                              uint32_t m, const float* qr, uint32_t cs, float q_add, float q_k1,
-                                              float* cd, uint32_t wib, uint32_t lane) {
-  const uint32_t t = lane & 3, g = wib * 8 + (lane >> 2);
-  const uint32_t iA = g, iB = g + 32;
-  const uint32_t* rA = stage + size_t(iA < m ? cpos[iA] : 0) * ix.rec_words;
-  const uint32_t* rB = stage + size_t(iB < m ? cpos[iB] : 0) * ix.rec_words;
-  const float2 p = estimate_pair_smem<BITS>(rA, rB, ix.dim, qr + t * cs, t);
-  const float dA = quad_butterfly(p.x), dB = quad_butterfly(p.y);
-  if (t == 0) {
-    constexpr float k1 = float((1u << BITS) - 1u);
-    if (iA < m)
-      cd[iA] = rabitq_finish(dA, __uint_as_float(rA[ix.code_words]), __uint_as_float(rA[ix.code_words + 1]), q_add,
-                             q_k1, k1);
-    if (iB < m)
-      cd[iB] = rabitq_finish(dB, __uint_as_float(rB[ix.code_words]), __uint_as_float(rB[ix.code_words + 1]), q_add,
-                             q_k1, k1);
-  }
-}
-
-// This warp's rounds of the exact rerank of `count` beam rows (the round body
-// of l2_rows_warp; warp w takes rounds w, w + 4, ...).
-__device__ __forceinline__ void coop_rerank(const DevLayout& ix, const float* __restrict__ q, const uint32_t* rows,
-                                            uint32_t count, float* out, uint32_t lane, uint32_t wib) {
-  const uint32_t t = lane & 3;
-  for (uint32_t r0 = 16 * wib; r0 < count; r0 += 16 * kCoopWarps) {
-    const uint32_t iA = r0 + (lane >> 2), iB = iA + 8;
-    float pA = 0.f, pB = 0.f;
-    if (iA < count) {
-      const float* xA = vec_row(ix, rows[iA] & ~kExpandedBit);
-      const float* xB = iB < count ? vec_row(ix, rows[iB] & ~kExpandedBit) : xA;
-      l2_quad_partial2(q, xA, xB, ix.dim, t, pA, pB);
-    }
-    const float tA = quad_butterfly(pA), tB = quad_butterfly(pB);
-    if (t == 0) {
-      if (iA < count) out[iA] = tA;
-      if (iB < count) out[iB] = tB;
-    }
-  }
+__host__ __device__ constexpr int search_max_regs(int npl, int rch, bool exact) {
+  return npl == 1 && (rch == 4 || exact) ? 96 : npl == 1 && rch == 8 ? 128 : (rch == 0 && !exact) ? 168 : 255;
 }
 
 // EXACT: exact_gpu (exact distances, no records; BITS and RCH unused) or
@@ -604,14 +463,12 @@ __device__ __forceinline__ void coop_rerank(const DevLayout& ix, const float* __
 // chunks of a RaBitQ record a lane holds in registers (0 = records too large:
 // they are loaded after the visited check instead).
 template <int BITS, int NPL, int RCH, bool EXACT>
-__global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kernel(const SearchArgs a) {
+__global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint32_t smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const DevLayout& ix = a.ix;
   constexpr uint32_t qlayout = EXACT ? kQueryRaw : (RCH == 0 && BITS != 8 ? kQueryChain : kQueryRot);
-  constexpr bool COOP = search_coop(BITS, RCH, EXACT);
-  const uint32_t warp_words = search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R, qlayout);
-  uint32_t* base = smem + (COOP ? 0 : size_t(wib) * warp_words);
+  uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R, qlayout);
   float* bd = reinterpret_cast<float*>(base);  // the beam: distances
   uint32_t* bi = base + a.cap_pad;            // and slot | expanded bit
   // exact_gpu: the query (qv); rabitq_gpu: q' (qr) in dimension or chain order
@@ -623,48 +480,15 @@ __global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kerne
   float* sd = reinterpret_cast<float*>(cid + 64 * NPL);
   uint32_t* sid = cid + 96 * NPL;
   uint32_t* htab = cid + 128 * NPL;
-  const uint32_t warp_slot = COOP ? blockIdx.x : blockIdx.x * (blockDim.x >> 5) + wib;
+  const uint32_t warp_slot = blockIdx.x * (blockDim.x >> 5) + wib;
   uint32_t* gtab = a.ovf ? a.ovf + size_t(warp_slot) * a.ovf_cap : nullptr;
   constexpr bool rabitq = !EXACT;  // the mode is a template parameter: each kernel holds one loop body
   const uint32_t dim = ix.dim, R = ix.R;
   const uint32_t nch = (ix.code_words + 2 + 3) >> 2;
   const float kInf = __int_as_float(0x7F800000);
-  // cooperative: the record stage (a record per adjacency-row position), the
-  // control words and the fresh candidates' row positions follow the leader's words
-  uint32_t* stage = smem + warp_words;
-  volatile uint32_t* ctl = stage + size_t(ix.R) * ix.rec_words;
-  uint32_t* cpos = const_cast<uint32_t*>(ctl) + kCoopCtlWords;
-  __shared__ __align__(8) uint64_t stage_bar;
-  uint32_t stage_uses = 0;  // leader: bulk-copy rounds started on stage_bar
-  if constexpr (COOP) {
-    if (threadIdx.x == 0) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&stage_bar)));
-      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    if (wib > 0) {
-      // helper warps: estimates and rerank rounds when the leader asks, until it says exit
-      const float* qr_l = reinterpret_cast<const float*>(base + 2 * a.cap_pad);
-      const uint32_t cs_l = chain_stride(a.dim_pad);
-      uint32_t* cid_l = base + 2 * a.cap_pad + 4 * cs_l;
-      float* cd_l = reinterpret_cast<float*>(cid_l + 32 * NPL);
-      for (;;) {
-        coop_sync();
-        const uint32_t cmd = ctl[0];
-        if (cmd == kCmdExit) return;
-        if (cmd == kCmdEstimate) {
-          stage_wait(smem_addr(&stage_bar), ctl[4]);  // already complete: orders the copies before the reads
-          coop_estimate<BITS == 8 ? 4 : BITS>(ix, stage, cpos, ctl[1], qr_l, cs_l, __uint_as_float(ctl[2]),
-                                              __uint_as_float(ctl[3]), cd_l, wib, lane);
-        } else {
-          // the leader put the query into its visited-table words
-          coop_rerank(ix, reinterpret_cast<const float*>(cid_l + 128 * NPL), base + a.cap_pad, ctl[1],
-                      reinterpret_cast<float*>(base), lane, wib);
-        }
-        coop_sync();
-      }
-    }
-  }
+  // RaBitQ records in registers are read under an L2 keep policy (1M 64-byte
+  // records fit L2), the rerank's full vectors under a stream policy
+  const uint64_t pol_keep = l2_policy_keep(), pol_stream = l2_policy_stream();
 
   for (;;) {
     uint32_t qi = 0;
@@ -756,28 +580,7 @@ __global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kerne
         const uint32_t j = lane + 32u * s;
         pf[s] = (guess != kEmptySlot && j < R) ? __ldg(adj_row(ix, guess) + j) : kEmptySlot;
       }
-      if constexpr (COOP) {
-        // every listed neighbour's record into the stage, at its row position
-        uint32_t nvalid = 0;
-#pragma unroll
-        for (int s = 0; s < NPL; ++s) nvalid += __popc(__ballot_sync(kFull, nbr[s] != kEmptySlot));
-        const uint32_t rbytes = ix.rec_words * 4;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        if (lane == 0)
-          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&stage_bar)),
-                       "r"(nvalid * rbytes)
-                       : "memory");
-        __syncwarp();
-#pragma unroll
-        for (int s = 0; s < NPL; ++s)
-          if (nbr[s] != kEmptySlot)
-            asm volatile(
-                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    smem_addr(stage + size_t(lane + 32u * s) * ix.rec_words)),
-                "l"(rec_row(ix, nbr[s])), "r"(rbytes), "r"(smem_addr(&stage_bar))
-                : "memory");
-        ++stage_uses;
-      } else if (RCH == 0 && rabitq && !hit) {
+      if (RCH == 0 && rabitq && !hit) {
         // wide records: every listed neighbour's record is brought towards L2
         // now (unless the previous hop already did, for a guessed row)
 #pragma unroll
@@ -793,7 +596,7 @@ __global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kerne
           if (nbr[s] != kEmptySlot) {
 #pragma unroll
             for (int c = 0; c < RCH; ++c)
-              if (c < int(nch)) rv[s][c] = __ldg(reinterpret_cast<const uint4*>(rec_row(ix, nbr[s])) + c);
+              if (c < int(nch)) rv[s][c] = ldg_hint(reinterpret_cast<const uint4*>(rec_row(ix, nbr[s])) + c, pol_keep);
           }
         }
       }
@@ -864,11 +667,6 @@ __global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kerne
         m += cnt;
         hcount += cnt;
       }
-      if constexpr (COOP) {
-        // the stage's copies land before anything else happens to it
-        if (!stage_wait(smem_addr(&stage_bar), (stage_uses - 1) & 1)) err |= kErrTimeout;
-        if (err & kErrTimeout) break;
-      }
       if (err & kErrCapacity) break;
       if (m == 0) {
         scan_from = best + 1;
@@ -885,7 +683,6 @@ __global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kerne
           if (fresh[s]) {
             const uint32_t pos = base_pos + __popc(bal & lanemask_lt());
             cid[pos] = nbr[s];
-            if (COOP) cpos[pos] = lane + 32u * s;
             if (RCH > 0 && rabitq) cd[pos] = estimate_regs<BITS, (RCH > 0 ? RCH : 1)>(rv[s], ix, qr, q_add, q_k1);
           }
           base_pos += __popc(bal);
@@ -894,18 +691,6 @@ __global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kerne
       __syncwarp();
       if (!rabitq) {
         l2_rows_warp(ix, qv, cid, m, cd, lane, 0xFFFFFFFFu);
-      } else if (COOP) {
-        if (lane == 0) {
-          ctl[0] = kCmdEstimate;
-          ctl[1] = m;
-          ctl[2] = __float_as_uint(q_add);
-          ctl[3] = __float_as_uint(q_k1);
-          ctl[4] = (stage_uses - 1) & 1;
-        }
-        __syncwarp();
-        coop_sync();
-        coop_estimate<BITS == 8 ? 4 : BITS>(ix, stage, cpos, m, qr, cs, q_add, q_k1, cd, 0, lane);
-        coop_sync();
       } else if (RCH == 0) {
         // wide records: 8 * kWideRecs per round, kWideRecs per lane quad
         // (candidates i, i + 8, ...), chains reduced with the tile butterfly
@@ -1053,18 +838,7 @@ __global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kerne
       __syncwarp();
       for (uint32_t j = lane; j < a.dim_pad; j += 32) qx[j] = j < dim ? qg[j] : 0.f;
       __syncwarp();
-      if constexpr (COOP) {
-        if (lane == 0) {
-          ctl[0] = kCmdRerank;
-          ctl[1] = nb;
-        }
-        __syncwarp();
-        coop_sync();
-        coop_rerank(ix, qx, bi, nb, bd, lane, 0);
-        coop_sync();
-      } else {
-        l2_rows_warp(ix, qx, bi, nb, bd, lane, ~kExpandedBit);
-      }
+      l2_rows_warp<true>(ix, qx, bi, nb, bd, lane, ~kExpandedBit, pol_stream);
       Cr = nb;
       __syncwarp();
       for (uint32_t p = lane; p < nb; p += 32) {
@@ -1101,12 +875,6 @@ __global__ void __maxnreg__(search_max_regs(BITS, NPL, RCH, EXACT)) search_kerne
       if (overflow) atomicAdd(a.work + 2, 1u);
     }
     __syncwarp();
-  }
-  if constexpr (COOP) {
-    // the helper warps leave with the leader
-    if (lane == 0) ctl[0] = kCmdExit;
-    __syncwarp();
-    coop_sync();
   }
 }
 
@@ -1244,20 +1012,13 @@ cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, boo
   }
 }
 
-bool search_cooperative(bool exact, uint32_t bits, uint32_t code_words) {
-  return search_coop(int(bits), record_chunks(code_words), exact);
-}
-
-size_t search_block_smem(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R, uint32_t rec_words,
-                         bool exact, uint32_t bits, uint32_t code_words, uint32_t wpb) {
-  const size_t words = search_warp_words(cap_pad, dim_pad, hcap, R, search_query_layout(exact, bits, code_words));
-  if (search_cooperative(exact, bits, code_words))  // one query: leader words, record stage, control, positions
-    return (words + size_t(R) * rec_words + kCoopCtlWords + 64) * 4;
-  return size_t(wpb) * words * 4;
+size_t search_block_smem(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R, bool exact, uint32_t bits,
+                         uint32_t code_words, uint32_t wpb) {
+  return size_t(wpb) * search_warp_words(cap_pad, dim_pad, hcap, R, search_query_layout(exact, bits, code_words)) * 4;
 }
 
 cudaError_t launch_search(const SearchArgs& a, uint32_t wpb, uint32_t blocks, cudaStream_t stream) {
-  const size_t smem = search_block_smem(a.cap_pad, a.dim_pad, a.hcap, a.ix.R, a.ix.rec_words, a.mode == 1, a.ix.bits,
+  const size_t smem = search_block_smem(a.cap_pad, a.dim_pad, a.hcap, a.ix.R, a.mode == 1, a.ix.bits,
                                         a.ix.code_words, wpb);
   const bool two = a.ix.R > 32;
   const int rch = record_chunks(a.ix.code_words);

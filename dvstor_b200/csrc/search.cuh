@@ -157,14 +157,9 @@ uint32_t search_query_layout(bool exact, uint32_t bits, uint32_t code_words);
 // wider than 128 bytes) rather than holding them in registers.
 bool search_wide_records(bool exact, uint32_t code_words);
 
-// Whether the search runs a query per CTA of four warps (rabitq_gpu with 1/2/4-bit
-// records wider than 128 bytes: the warps share the estimates and the rerank).
-bool search_cooperative(bool exact, uint32_t bits, uint32_t code_words);
-
-// Dynamic shared memory of a search block of `wpb` warps (a cooperative block
-// is one query of four warps whatever `wpb`).
-size_t search_block_smem(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R, uint32_t rec_words,
-                         bool exact, uint32_t bits, uint32_t code_words, uint32_t wpb);
+// Dynamic shared memory of a search block of `wpb` warps.
+size_t search_block_smem(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R, bool exact, uint32_t bits,
+                         uint32_t code_words, uint32_t wpb);
 
 }  // namespace dvs
 

@@ -7,9 +7,9 @@ operation runs its own Vamana loop with its own tiny GPU launches
 client threads, tools/dvstor_breakdown_benchmark.cc:511-526).  On a B200 one
 warp runs a whole query, so the server batches instead: ``BatchingServer``
 collects the operations that clients have submitted, runs all pending queries
-as one ``dvs_search`` call and all pending inserts as one ``dvs_insert`` call,
-and hands every client its own result.  An operation's latency is its queue
-wait plus the batch it rode in.
+as one ``dvs_search`` call and all pending inserts as one ``dvs_insert`` call
+(the two batches on the GPU at once), and hands every client its own result.
+An operation's latency is its queue wait plus the batch it rode in.
 
 ``Breakdown`` records one sample per operation (enqueue, start, finish, the
 GPU time of its batch) and writes the reference's breakdown JSON
@@ -152,10 +152,12 @@ class _Op:
 
 
 class BatchingServer:
-    """One worker thread owns the index; client threads call ``search`` and
-    ``insert`` concurrently and block until their own operation is done.  The
-    worker alternates: every pending query as one ``dvs_search`` batch, then
-    every pending insert as one ``dvs_insert`` batch."""
+    """Client threads call ``search`` and ``insert`` concurrently and block until
+    their own operation is done.  Two worker threads batch them: one runs every
+    pending query as one ``dvs_search`` call, the other every pending insert as
+    one ``dvs_insert`` call.  The library lets a search run on the GPU while an
+    insert step does (inserts have their own scratch and stream), so queries
+    do not wait behind an insert batch."""
 
     def __init__(self, index, k: int, beam_width: int, mode: str = "rabitq_gpu", beam_width_construction: int = 128,
                  alpha: float = 1.2, max_batch: int = 4096, breakdown: Breakdown | None = None):
@@ -166,8 +168,10 @@ class BatchingServer:
         self.queries, self.inserts = [], []
         self.stopping = False
         self.batches = {"query": 0, "insert": 0}
-        self.worker = threading.Thread(target=self._run, name="dvs-batcher", daemon=True)
-        self.worker.start()
+        self.workers = [threading.Thread(target=self._run, args=(kind,), name=f"dvs-{kind}", daemon=True)
+                        for kind in ("query", "insert")]
+        for w in self.workers:
+            w.start()
 
     # ---- client side ----
     def search(self, query):
@@ -185,7 +189,7 @@ class BatchingServer:
             if self.stopping:
                 raise RuntimeError("server stopped")
             (self.queries if op.kind == "query" else self.inserts).append(op)
-            self.cv.notify()
+            self.cv.notify_all()
         op.done.wait()
         if op.error is not None:
             raise op.error
@@ -193,8 +197,9 @@ class BatchingServer:
     def close(self):
         with self.cv:
             self.stopping = True
-            self.cv.notify()
-        self.worker.join()
+            self.cv.notify_all()
+        for w in self.workers:
+            w.join()
 
     # ---- worker ----
     def _take(self, lst):
@@ -202,20 +207,17 @@ class BatchingServer:
         del lst[:len(ops)]
         return ops
 
-    def _run(self):
+    def _run(self, kind):
+        pending = self.queries if kind == "query" else self.inserts
+        run = self._run_queries if kind == "query" else self._run_inserts
         while True:
             with self.cv:
-                while not self.queries and not self.inserts and not self.stopping:
+                while not pending and not self.stopping:
                     self.cv.wait()
-                if self.stopping and not self.queries and not self.inserts:
+                if self.stopping and not pending:
                     return
-                qs = self._take(self.queries)
-            if qs:
-                self._run_queries(qs)
-            with self.cv:
-                ins = self._take(self.inserts)
-            if ins:
-                self._run_inserts(ins)
+                ops = self._take(pending)
+            run(ops)
 
     def _finish(self, ops, err):
         for op in ops:

@@ -309,8 +309,12 @@ typedef struct dvs_insert_stats {
  * vector is quantized by the GPU quantizer (rabitq_quantize_single_kernel),
  * and reverse edges are added in insert order (append, or RobustPrune of a
  * full list).  Steps of one vector reproduce the reference's sequential
- * insert.  Waits for work in flight on the index's devices first and holds the
- * index lock while it runs. */
+ * insert.  Inserts run one at a time, on their own stream and scratch; other
+ * threads' searches run meanwhile (they see the graph as the insert kernels
+ * leave it, every step's node count once the step is done, as concurrent
+ * readers of the reference's graph do).  When the arrays must grow, work in
+ * flight on the devices finishes first (dvs_reserve grows them ahead of
+ * time). */
 dvs_status dvs_insert(dvs_index* index, const float* h_vectors, const uint32_t* h_ids, uint32_t n, uint32_t dim,
                       const dvs_insert_params* params, dvs_insert_stats* stats);
 

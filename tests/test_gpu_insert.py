@@ -116,3 +116,48 @@ def test_insert_rejects_bad_input(gpu, oracle, tmp_path):
     with gpu.Index(prefix, devices=(0, 0), placement="shard") as sh:
         with pytest.raises(gpu.DvsError, match="replicated"):
             sh.insert(X[:1])
+
+
+def test_searches_run_while_inserting(gpu, oracle, tmp_path):
+    """Searches from other threads while an insert runs (inserts have their own
+    scratch and stream and hold the index lock only between steps): every
+    search succeeds with ids of the index, and the inserts leave the device
+    index equal to the oracle's, as without searches."""
+    import threading
+
+    X = normalized_gaussian(3000, 48, 46)
+    orc = oracle.build_index(X[:1500], R=16, L=32)
+    prefix = write_oracle_index(oracle, orc, str(tmp_path / "conc"), 1)
+    Q = normalized_gaussian(200, 48, 47)
+    new_ids = np.arange(90_000, 91_500, dtype=np.uint32)
+    with gpu.Index(prefix) as ix:
+        ix.reserve(3000)
+        stop = threading.Event()
+        seen = {"searches": 0, "errors": []}
+
+        def searcher():
+            while True:
+                try:
+                    ids, d = ix.search(Q, 10, 48)
+                    ok = (ids != gpu.EMPTY) & ((ids < 1500) | ((ids >= 90_000) & (ids < 91_500)))
+                    assert ok.all() and np.isfinite(d).all()
+                    seen["searches"] += 1
+                except Exception as e:  # reported below, in the test's thread
+                    seen["errors"].append(e)
+                    return
+                if stop.is_set():
+                    return
+
+        th = [threading.Thread(target=searcher) for _ in range(2)]
+        for t in th:
+            t.start()
+        try:
+            ix.insert(X[1500:], new_ids, beam_width_construction=64, alpha=1.2, max_batch=100)
+        finally:
+            stop.set()
+            for t in th:
+                t.join()
+        assert not seen["errors"], seen["errors"][:1]
+        assert seen["searches"] > 0
+        orc.insert(X[1500:], new_ids, beam_width_construction=64, alpha=1.2, max_batch=100)
+        _assert_same_index(ix, orc)

@@ -324,7 +324,7 @@ def test_sharded_rejects_bad_device_counts(gpu, cases):
     assert e.value.name == "DVS_ERR_ARG"
 
 
-@pytest.mark.parametrize("name,L", [("gauss96", 64), ("d256r48", 48)])
+@pytest.mark.parametrize("name,L", [("gauss96", 64), ("d256r48", 48), ("d960r48", 200)])
 def test_tensor_core_rotation_search(gpu, oracle, cases, name, L):
     """With the rotation on tensor cores the rest of the path is unchanged: the
     search equals the oracle's knn fed the GPU's rotated queries and factors."""
