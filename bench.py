@@ -571,7 +571,7 @@ def run_ours(args):
         rec = recall(g_ids, gt)
         if args.parity_queries:
             par = parity_check(ix, X, Qpool[:args.parity_queries], k, L, args.search_mode, device, args.rotation)
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and dist.world == 1:  # timed at N=1 only
             cpu = cpu_baseline(X, np.concatenate([gtq, Qpool[1000:]]), L, k, args.cpu_seconds, gt_q=None)
             ids_cpu, _ = O.cpu_beam_search_batch(X.X, X.adj, X.medoid, gtq, L, k)
             cpu["recall_at_10"] = recall(ids_cpu, gt)
