@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <map>
 #include <mutex>
@@ -181,10 +182,11 @@ dvs_status grow_rows(Device& d, uint64_t rows);
 struct dvs_index {
   dvs::HostIndex host;              // kept for downloads and metadata
   std::vector<dvs::Device> devs;
-  uint32_t hop_limit = 0;
-  uint32_t slots_per_entry = 0;  // 0 = sized for the most resident warps (kSlotsMin..kSlotsMax)
-  bool kernel_timing = false;
-  dvs_rotation rotation = DVS_ROTATION_EXACT;
+  // settings: written under mu, read by searches and by the insert thread
+  std::atomic<uint32_t> hop_limit{0};
+  std::atomic<uint32_t> slots_per_entry{0};  // 0 = sized for the most resident warps (kSlotsMin..kSlotsMax)
+  std::atomic<bool> kernel_timing{false};
+  std::atomic<dvs_rotation> rotation{DVS_ROTATION_EXACT};
   // mu guards the host state (device layouts, scratch, settings); an insert
   // holds it only to grow the arrays and to publish a step, and ins_mu for the
   // whole call, so searches proceed while an insert step runs on the GPU

@@ -7,10 +7,10 @@
 // in tensor memory (the dropped Qlo Plo term is ~2^-22 relative).
 //
 // P is split once per index and device (tc_rotation_prepare): hi and lo planes,
-// K padded with zeros to a multiple of 32, read by TMA.  One CTA of 4 warps
-// computes a 128-query x NT-column tile (NT <= 256, a multiple of 16) in
-// 32-float K chunks through a two-stage ring of shared-memory tiles in the
-// 128-byte-swizzled K-major layout the MMA reads:
+// K padded with zeros to a multiple of 32, read by TMA.  One CTA computes a
+// 128-query x NT-column tile (NT <= 256, a multiple of 16) in 32-float K chunks
+// through a two-stage ring of shared-memory tiles in the 128-byte-swizzled
+// K-major layout the MMA reads:
 //   * thread 0 starts the TMA copy of the chunk's P hi/lo tiles (this GPU's
 //     memory, no multicast) on the stage's mbarrier;
 //   * every thread splits the query values it loaded during the previous
@@ -18,8 +18,9 @@
 //   * thread 0 waits for the TMA bytes, issues 4 K-steps x 3 MMAs (M=128,
 //     N=NT, K=8) into the TMEM accumulator and commits them to the stage's
 //     MMA mbarrier, which frees the stage two chunks later.
-// After the last chunk every warp reads its 32 TMEM lanes with tcgen05.ld and
-// stores its rows.  Every mbarrier wait is bounded: on expiry the CTA records
+// Eight warps share the splitting (16 query rows each).  After the last chunk
+// the two warps of each 32-lane TMEM row group read alternate 16-column blocks
+// with tcgen05.ld and store them.  Every mbarrier wait is bounded: on expiry the CTA records
 // an error, waits (bounded) for its copies and MMAs in flight, frees its TMEM
 // and exits.
 
@@ -39,6 +40,8 @@ namespace {
 constexpr uint32_t kTileM = 128;     // queries per CTA (MMA M)
 constexpr uint32_t kChunk = 32;      // K floats per smem chunk (one 128-byte swizzle row)
 constexpr uint32_t kStages = 2;
+constexpr uint32_t kWarps = 8;       // two warpgroups: each row group of 32 TMEM lanes has two warps
+constexpr uint32_t kRowsPerWarp = kTileM / kWarps;
 constexpr uint32_t kWaitLimit = 1u << 20;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -119,7 +122,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kWarps * 32, 1)
     rotate_tc_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
                      const float* __restrict__ Q, uint32_t q_stride, uint32_t q_vec4, float* __restrict__ out,
                      uint32_t out_stride, uint32_t out_vec4, uint32_t dim, uint32_t kp, uint32_t nq, uint32_t nt,
@@ -156,14 +159,15 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t idesc = instr_desc_tf32(nt);
   const uint32_t nchunks = kp / kChunk;
 
-  // this thread's query values of one chunk: rows warp*32 + 4i + lane/8, floats 4*(lane%8) .. +3
+  // this thread's query values of one chunk: rows warp*16 + 4i + lane/8, floats 4*(lane%8) .. +3
   const uint32_t k4 = lane & 7;
-  float4 ra[8];
+  constexpr int kRowIters = kRowsPerWarp / 4;
+  float4 ra[kRowIters];
   auto load_a = [&](uint32_t c) {
     const uint32_t k = c * kChunk + 4 * k4;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t q = q0 + warp * 32 + 4 * i + (lane >> 3);
+    for (int i = 0; i < kRowIters; ++i) {
+      const uint32_t q = q0 + warp * kRowsPerWarp + 4 * i + (lane >> 3);
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (q < nq) {
         const float* row = Q + size_t(q) * q_stride;
@@ -200,8 +204,8 @@ __global__ void __launch_bounds__(128, 1)
       ++tma_started[s];
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t row = warp * 32 + 4 * i + (lane >> 3);
+    for (int i = 0; i < kRowIters; ++i) {
+      const uint32_t row = warp * kRowsPerWarp + 4 * i + (lane >> 3);
       const float4 x = ra[i];
       float4 hi, lo;
       hi.x = to_tf32(x.x);
@@ -245,12 +249,15 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
 
   if (!failed) {
+    // warp w reads TMEM lanes 32 (w mod 4) .. +31 (its rows); the two warps of
+    // a row group take alternate 16-column blocks
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t row = warp * 32 + lane;
+    const uint32_t group = warp & 3, half = warp >> 2;
+    const uint32_t row = group * 32 + lane;
     const uint32_t q = q0 + row;
-    for (uint32_t c0 = 0; c0 < nt; c0 += 16) {
+    for (uint32_t c0 = 16 * half; c0 < nt; c0 += 32) {
       uint32_t v[16];
-      const uint32_t taddr = tmem + ((warp * 32) << 16) + c0;
+      const uint32_t taddr = tmem + ((group * 32) << 16) + c0;
       asm volatile(
           "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
           : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
@@ -376,7 +383,7 @@ cudaError_t launch_prepare_tc(const float* queries, uint32_t q_stride, const TcR
   const uint32_t q_vec4 = (q_stride % 4 == 0 && reinterpret_cast<uintptr_t>(queries) % 16 == 0) ? 1u : 0u;
   const uint32_t o_vec4 = (qrot_stride % 4 == 0 && reinterpret_cast<uintptr_t>(qrot) % 16 == 0) ? 1u : 0u;
   const dim3 grid((nq + kTileM - 1) / kTileM, (dim + nt - 1) / nt);
-  rotate_tc_kernel<<<grid, 128, smem, stream>>>(t.map_hi, t.map_lo, queries, q_stride, q_vec4, qrot, qrot_stride,
+  rotate_tc_kernel<<<grid, kWarps * 32, smem, stream>>>(t.map_hi, t.map_lo, queries, q_stride, q_vec4, qrot, qrot_stride,
                                                 o_vec4, dim, t.kp, nq, nt, err);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
