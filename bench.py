@@ -18,6 +18,10 @@ vectors) is larger than L2, which is not flushed between steps.
 `--impl reference` times the reference's CPU Vamana beam search (restated in
 oracle/, the reference's own code cannot be built here) on the host cores.
 
+The query rotation runs on the tcgen05 tensor cores (`--rotation tensor`, the
+default; the parity leg then gives the oracle the GPU's rotated queries) or on
+the FP32 pipe in the oracle's own order (`--rotation exact`).
+
 Other rows of the path: `--search-mode exact_gpu` (exact L2 for every
 candidate), `--bits 1|2|8` (the index built with that code width),
 `--workload` / `--n` / `--batch` / `--k` / `--beam-width` for the other
@@ -72,8 +76,9 @@ def parse_args():
     ap.add_argument("--alpha", type=float, default=1.2)
     ap.add_argument("--placement", choices=["replicate", "shard"], default="replicate",
                     help="shard: one process over --gpus devices, the index split by slot (run without torchrun)")
-    ap.add_argument("--rotation", choices=["exact", "tensor"], default="exact",
-                    help="query rotation: fp32 in the oracle's fixed order, or tcgen05 tensor cores (3xTF32)")
+    ap.add_argument("--rotation", choices=["exact", "tensor"], default="tensor",
+                    help="query rotation: tcgen05 tensor cores (3xTF32, the default), or fp32 in the oracle's fixed "
+                         "order")
     ap.add_argument("--metric", choices=["l2", "ip"], default=None,
                     help="index metric (default: ip for --mode mixed, else l2)")
     ap.add_argument("--clients", type=int, default=16, help="--mode mixed: client threads per GPU")
@@ -349,6 +354,18 @@ def bytes_per_query(dim, R, bits, k, H, E, Cr, nq, mode="rabitq_gpu"):
     return 4 * dim + H * (4 * R + 1) + E * s_code + Cr * 4 * dim + 4 * dim * dim / nq + 8 * k
 
 
+def launches_per_search(args, dim) -> int:
+    """This library's kernels per search call: the search kernel, and for
+    rabitq_gpu the query prepare (the tensor-core rotation and the factors
+    kernel; the FP32 rotation with its factors in one kernel up to 128 dims,
+    in two above)."""
+    if args.search_mode == "exact_gpu":
+        return 1
+    if args.rotation == "tensor" or dim > 128:
+        return 3
+    return 2
+
+
 def metric_name(k, L, mode):
     """The headline metric; exact_gpu runs name their mode."""
     return f"queries/sec at recall@10 parity (k={k}, L={L}{', exact_gpu' if mode == 'exact_gpu' else ''})"
@@ -596,7 +613,7 @@ def run_ours(args):
                                        "E_max": int(c[:, 1].max())}},
             "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": B * wp["dim"] * 4,
                     "d2h_bytes_per_step": B * k * 8},
-            "gpu_launches": (1 if args.search_mode == "exact_gpu" else 2) * args.steps,
+            "gpu_launches": launches_per_search(args, wp["dim"]) * args.steps,
             "clocks": clocks,
             "recall_at_10": rec,
             "parity": par,
@@ -624,6 +641,7 @@ def run_sharded(args):
     k, B = args.k, args.batch
     prefix = ensure_index(args, wp, 0, dist)
     ix = D.Index(prefix, devices=tuple(range(ngpu)), placement="shard")
+    ix.set_rotation(args.rotation)
     info = ix.info
     nsteps = args.warmup + args.steps
     Qpool = datasets.queries_for(args.workload, B * ngpu * nsteps)
@@ -699,7 +717,8 @@ def run_sharded(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "n": wp["n"], "dim": wp["dim"], "R": wp["R"], "build_L": wp["build_L"],
                    "rabitq_bits": args.bits, "search_mode": args.search_mode, "k": k, "beam_width": L,
-                   "queries_per_step_per_gpu": B, "parallelism": f"shard x{ngpu} (one process, peer HBM reads)",
+                   "rotation": args.rotation, "queries_per_step_per_gpu": B,
+                   "parallelism": f"shard x{ngpu} (one process, peer HBM reads)",
                    "l2": f"index {index_device_bytes(info) / 1e9:.2f} GB split over {ngpu} GPUs, not flushed"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * ngpu, "unit": "GB/s",
                      "frac": achieved / (peak * ngpu), "traffic": None,
@@ -707,7 +726,7 @@ def run_sharded(args):
                      "kernel_ms": search_avg_ms, "bytes_per_query": bq, "per_query": {"H": H, "E": E, "C_r": Cr}},
         "e2e": {"value": e2e, "unit": "queries/s", "h2d_bytes_per_step": B * ngpu * wp["dim"] * 4,
                 "d2h_bytes_per_step": B * ngpu * k * 8},
-        "gpu_launches": (1 if args.search_mode == "exact_gpu" else 2) * args.steps * ngpu,
+        "gpu_launches": launches_per_search(args, wp["dim"]) * args.steps * ngpu,
         "clocks": clocks,
         "recall_at_10": rec,
         "cpu_baseline": None,
@@ -811,6 +830,7 @@ def run_mixed(args):
     k = args.k
     prefix = ensure_index(args, wp, device, dist)
     ix = D.Index(prefix, devices=(device,))
+    ix.set_rotation(args.rotation)
     n0 = int(ix.info.num_vectors)
     ix.reserve(n0 + args.reserve)
     bd = Breakdown()

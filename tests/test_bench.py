@@ -69,3 +69,12 @@ def test_index_cache_tag_follows_the_bit_width():
     wp = bench.workload_params(a4.workload)
     assert bench.index_prefix(a4, wp) != bench.index_prefix(a8, wp)
     assert "_b8_" in bench.index_prefix(a8, wp)
+
+
+def test_launch_count_follows_the_prepare_kernels():
+    # search kernel + prepare: tensor-core rotation and factors (2), FP32 rotation with
+    # factors in one kernel up to 128 dims (1) or two above; exact_gpu has no prepare
+    assert bench.launches_per_search(_args(), 96) == 3
+    assert bench.launches_per_search(_args("--rotation", "exact"), 96) == 2
+    assert bench.launches_per_search(_args("--rotation", "exact"), 960) == 3
+    assert bench.launches_per_search(_args("--search-mode", "exact_gpu"), 96) == 1
