@@ -72,3 +72,32 @@ def test_gpu_builder_rejects_bad_arguments(gpu, tmp_path):
     bad[3, 3] = np.inf
     with pytest.raises(gpu.DvsError):
         build_index(bad, None)
+
+
+def test_gpu_builder_inner_product_index(gpu, oracle, tmp_path):
+    """metric "ip" (the reference builder's --ip-dist) on unit-norm data: the
+    same graph and records as the L2 build, the metadata says "ip", and a
+    search (1 - dot medoid seed) equals the oracle's knn with the IP seed on
+    the same files."""
+    import json
+
+    from dvstor_b200.builder import build_index
+
+    X = normalized_gaussian(3000, 48, 9)
+    st_l2, adj_l2, rec_l2 = build_index(X, str(tmp_path / "l2" / "idx"), R=24, beam_width=48, batch_cap=64,
+                                        return_arrays=True)
+    pre = str(tmp_path / "ip" / "idx")
+    st_ip, adj_ip, rec_ip = build_index(X, pre, R=24, beam_width=48, batch_cap=64, return_arrays=True, metric="ip")
+    np.testing.assert_array_equal(adj_ip, adj_l2)
+    np.testing.assert_array_equal(rec_ip, rec_l2)
+    assert json.load(open(pre + ".meta.json"))["distance"] == "ip"
+    orc = oracle.read_index(pre)
+    assert orc.metric == "ip"
+    Q = normalized_gaussian(200, 48, 10)
+    with gpu.Index(pre) as ix:
+        assert ix.info.metric == 1
+        ids, d = ix.search(Q, 10, 48)
+    o_ids, o_d, _, b_ids, b_d = orc.knn(Q, 10, 48, beam_cap=48 + 64)
+    from conftest import assert_results_match
+
+    assert_results_match(ids, d, o_ids, o_d, b_ids, b_d)
