@@ -228,20 +228,18 @@ __device__ __forceinline__ void code_word(uint32_t word, uint32_t wi, int e, con
   }
 }
 
-// Chain t of NR records' estimates (ids c[r]; a record may repeat c[0] when
-// the round has fewer), computed by lane t of a lane quad: the reference
-// kernel's own tile-of-4 split (lane t sums dims j = t mod 4 for B in {1,2,4},
-// char4 steps c = t mod 4 for B = 8), each chain in ascending order.  Used for
-// records wider than 128 bytes.  The NR chains are independent, so their
-// loads and FMAs interleave; each q' read serves all of them; KB chunks of
-// every record are in flight per batch.  For B in {1,2,4} `q` is this lane's
-// chain of the chain-major q' (position p = dim 4p + t), for B = 8 the
-// dimension-order q'.  Lane 0 also returns the records' add and rescale
+// Chain t of NR records' 8-bit estimates (ids c[r]; a record may repeat c[0]
+// when the round has fewer), computed by lane t of a lane quad: the reference
+// kernel's own tile-of-4 split (lane t sums the char4 steps c = t mod 4), each
+// chain in ascending order.  Used for 8-bit records wider than 128 bytes.  The
+// NR chains are independent, so their loads and FMAs interleave; each q' read
+// serves all of them; KB words of every record are in flight per batch.  `q`
+// is q' in dimension order.  Lane 0 also returns the records' add and rescale
 // factors.
-template <int BITS, int NR, int KB>
-__device__ __forceinline__ void estimate_quad_chains(const DevLayout& ix, const uint32_t (&c)[NR],
-                                                     const float* __restrict__ q, uint32_t t, float (&s)[NR],
-                                                     float (&f)[NR][2]) {
+template <int NR, int KB>
+__device__ __forceinline__ void estimate_quad_chains8(const DevLayout& ix, const uint32_t (&c)[NR],
+                                                      const float* __restrict__ q, uint32_t t, float (&s)[NR],
+                                                      float (&f)[NR][2]) {
   const uint32_t* r[NR];
 #pragma unroll
   for (int k = 0; k < NR; ++k) {
@@ -252,81 +250,98 @@ __device__ __forceinline__ void estimate_quad_chains(const DevLayout& ix, const 
       f[k][1] = __uint_as_float(__ldg(r[k] + ix.code_words + 1));
     }
   }
-  if constexpr (BITS == 8) {
-    // lane t takes words t, t+4, ...: KB of each record in flight per batch
-    const uint32_t nw = ix.dim >> 2;
-    for (uint32_t w0 = t; w0 < nw; w0 += 4 * KB) {
-      uint32_t a[NR][KB];
+  // lane t takes words t, t+4, ...: KB of each record in flight per batch
+  const uint32_t nw = ix.dim >> 2;
+  for (uint32_t w0 = t; w0 < nw; w0 += 4 * KB) {
+    uint32_t a[NR][KB];
 #pragma unroll
-      for (int j = 0; j < KB; ++j)
-        if (w0 + 4 * j < nw) {
+    for (int j = 0; j < KB; ++j)
+      if (w0 + 4 * j < nw) {
 #pragma unroll
-          for (int k = 0; k < NR; ++k) a[k][j] = __ldg(r[k] + w0 + 4 * j);
-        }
+        for (int k = 0; k < NR; ++k) a[k][j] = __ldg(r[k] + w0 + 4 * j);
+      }
 #pragma unroll
-      for (int j = 0; j < KB; ++j)
-        if (w0 + 4 * j < nw) {
-          const float4 q4 = *reinterpret_cast<const float4*>(q + 4 * (w0 + 4 * j));
+    for (int j = 0; j < KB; ++j)
+      if (w0 + 4 * j < nw) {
+        const float4 q4 = *reinterpret_cast<const float4*>(q + 4 * (w0 + 4 * j));
 #pragma unroll
-          for (int k = 0; k < NR; ++k) s[k] = __fadd_rn(s[k], rabitq_char4(a[k][j], q4));
-        }
-    }
-  } else {
-    // a 16-byte chunk holds kPer = 32/B dims of each of the 4 chains: positions
-    // kPer*ch .. kPer*ch + kPer-1 of this lane's chain, word e giving kPer/4 of them
-    constexpr uint32_t kPer = 32 / BITS, kMask = (1u << BITS) - 1u;
-    const uint32_t nch = (ix.dim / kPer) >> 2;  // chunks whose every dim is < dim
-    const uint32_t sh0 = BITS * t;
-    for (uint32_t ch = 0; ch < nch; ch += KB) {
-      uint4 v[NR][KB];
+        for (int k = 0; k < NR; ++k) s[k] = __fadd_rn(s[k], rabitq_char4(a[k][j], q4));
+      }
+  }
+}
+
+// Chains 2h and 2h + 1 of the 1/2/4-bit estimate of record g, computed by lane
+// h of a lane pair: the reference kernel's tile-of-4 chains (chain c sums dims
+// j = c mod 4 in ascending order), both on one packed two-lane FP32 FMA per
+// position (each lane of a packed FMA is the same fmaf).  `q` is this lane's
+// half of the pair-major q'; the pair's other lane returns chains 2(1-h) and
+// 2(1-h) + 1.  KB 16-byte chunks of the record are in flight per batch.
+template <int BITS, int KB>
+__device__ __forceinline__ float2 estimate_pair_chains(const DevLayout& ix, uint32_t g, const float* __restrict__ q,
+                                                       uint32_t h) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(rec_row(ix, g));
+  constexpr uint32_t kPer = 32 / BITS, kMask = (1u << BITS) - 1u;
+  const float2 neg_magic = make_float2(-8388608.0f, -8388608.0f);
+  float2 s = make_float2(0.f, 0.f);
+  // a word holds kPer dims, kPer / 4 positions of each chain: this lane takes
+  // dims n = 4i + 2h and 4i + 2h + 1 of it (position i of its two chains)
+  const uint32_t nch = (ix.dim / kPer) >> 2;  // 16-byte chunks whose every dim is < dim
+  for (uint32_t ch = 0; ch < nch; ch += KB) {
+    uint4 v[KB];
 #pragma unroll
-      for (int j = 0; j < KB; ++j)
-        if (ch + j < nch) {
+    for (int j = 0; j < KB; ++j)
+      if (ch + j < nch) v[j] = __ldg(reinterpret_cast<const uint4*>(r) + ch + j);
 #pragma unroll
-          for (int k = 0; k < NR; ++k) v[k][j] = __ldg(reinterpret_cast<const uint4*>(r[k]) + ch + j);
-        }
+    for (int j = 0; j < KB; ++j) {
+      if (ch + j < nch) {
 #pragma unroll
-      for (int j = 0; j < KB; ++j) {
-        if (ch + j < nch) {
-          float qf[kPer];
-          const float4* q4 = reinterpret_cast<const float4*>(q + (ch + j) * kPer);
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t w = e == 0 ? v[j].x : e == 1 ? v[j].y : e == 2 ? v[j].z : v[j].w;
+          const float* qw = q + 2 * ((ch + j) * 4 + e) * (kPer / 4);
+          if constexpr (BITS == 4) {
+            // dims 4i + 2h, 4i + 2h + 1 are the low and high nibble of byte 2i + h;
+            // PRMT places each under the exponent of 2^23, the subtraction
+            // leaves it exact
+            const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+            const float4 qv = *reinterpret_cast<const float4*>(qw);
+            const float2 c0 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u + h)),
+                                                     __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u + h))),
+                                         neg_magic);
+            s = __ffma2_rn(c0, make_float2(qv.x, qv.y), s);
+            const float2 c1 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7442u + h)),
+                                                     __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7442u + h))),
+                                         neg_magic);
+            s = __ffma2_rn(c1, make_float2(qv.z, qv.w), s);
+          } else {
 #pragma unroll
-          for (uint32_t g = 0; g < kPer / 4; ++g) {
-            const float4 fq = q4[g];
-            qf[4 * g] = fq.x;
-            qf[4 * g + 1] = fq.y;
-            qf[4 * g + 2] = fq.z;
-            qf[4 * g + 3] = fq.w;
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-#pragma unroll
-            for (uint32_t i = 0; i < kPer / 4; ++i) {
-              const uint32_t sh = sh0 + 4 * BITS * i;
-              const float qv = qf[e * (kPer / 4) + i];
-#pragma unroll
-              for (int k = 0; k < NR; ++k) {
-                const uint32_t w = e == 0 ? v[k][j].x : e == 1 ? v[k][j].y : e == 2 ? v[k][j].z : v[k][j].w;
-                s[k] = __fmaf_rn(small_u2f((w >> sh) & kMask), qv, s[k]);
-              }
+            for (uint32_t i = 0; i < kPer / 4; i += 2) {
+              const float4 qv = *reinterpret_cast<const float4*>(qw + 2 * i);
+              const uint32_t n0 = 4 * i + 2 * h, n1 = n0 + 4;
+              const float2 c0 = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | ((w >> (BITS * n0)) & kMask)),
+                                                       __uint_as_float(0x4B000000u | ((w >> (BITS * (n0 + 1))) & kMask))),
+                                           neg_magic);
+              s = __ffma2_rn(c0, make_float2(qv.x, qv.y), s);
+              const float2 c1 = __fadd2_rn(make_float2(__uint_as_float(0x4B000000u | ((w >> (BITS * n1)) & kMask)),
+                                                       __uint_as_float(0x4B000000u | ((w >> (BITS * (n1 + 1))) & kMask))),
+                                           neg_magic);
+              s = __ffma2_rn(c1, make_float2(qv.z, qv.w), s);
             }
           }
         }
       }
     }
-    // words past the last whole chunk, the partial last word included
-    for (uint32_t wi = nch * 4; wi * kPer < ix.dim; ++wi) {
-      uint32_t w[NR];
-#pragma unroll
-      for (int k = 0; k < NR; ++k) w[k] = __ldg(r[k] + wi);
-      const uint32_t j0 = wi * kPer;
-      for (uint32_t n = t; n < kPer && j0 + n < ix.dim; n += 4) {
-        const float qv = q[(j0 + n) >> 2];
-#pragma unroll
-        for (int k = 0; k < NR; ++k) s[k] = __fmaf_rn(small_u2f((w[k] >> (BITS * n)) & kMask), qv, s[k]);
-      }
+  }
+  // words past the last whole chunk, the partial last word included
+  for (uint32_t wi = nch * 4; wi * kPer < ix.dim; ++wi) {
+    const uint32_t w = __ldg(r + wi), j0 = wi * kPer;
+    for (uint32_t i = 0; i < kPer / 4; ++i) {
+      const uint32_t n = 4 * i + 2 * h;
+      const float* qp = q + 2 * ((j0 + n) >> 2);
+      if (j0 + n < ix.dim) s.x = __fmaf_rn(small_u2f((w >> (BITS * n)) & kMask), qp[0], s.x);
+      if (j0 + n + 1 < ix.dim) s.y = __fmaf_rn(small_u2f((w >> (BITS * (n + 1))) & kMask), qp[1], s.y);
     }
   }
+  return s;
 }
 
 // Asks L2 for every 128-byte line of node g's RaBitQ record (wide records:
@@ -441,9 +456,9 @@ __device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n,
   return lo;
 }
 
-// Wide records: records per lane quad per round and 16-byte chunks of each in
-// flight per batch.
-constexpr int kWideRecs = 3, kWideBatch = 6;
+// Wide records: 8-bit records per lane quad per round and words of each in
+// flight per batch; 16-byte chunks of a 1/2/4-bit record in flight per batch.
+constexpr int kWideRecs = 3, kWideBatch = 6, kPairBatch = 10;
 
 // Register cap of a search_kernel instantiation.  R <= 32 with records of up
 // to 64 bytes in registers (and exact_gpu): 96, five warps per SM
@@ -467,15 +482,14 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
   extern __shared__ __align__(16) uint32_t smem[];
   const uint32_t lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const DevLayout& ix = a.ix;
-  constexpr uint32_t qlayout = EXACT ? kQueryRaw : (RCH == 0 && BITS != 8 ? kQueryChain : kQueryRot);
+  constexpr uint32_t qlayout = EXACT ? kQueryRaw : (RCH == 0 && BITS != 8 ? kQueryPair : kQueryRot);
   uint32_t* base = smem + size_t(wib) * search_warp_words(a.cap_pad, a.dim_pad, a.hcap, ix.R, qlayout);
   float* bd = reinterpret_cast<float*>(base);  // the beam: distances
   uint32_t* bi = base + a.cap_pad;            // and slot | expanded bit
-  // exact_gpu: the query (qv); rabitq_gpu: q' (qr) in dimension or chain order
+  // exact_gpu: the query (qv); rabitq_gpu: q' (qr) in dimension order or pair-major
   float* qv = reinterpret_cast<float*>(base + 2 * a.cap_pad);
   float* qr = qv;
-  const uint32_t cs = chain_stride(a.dim_pad);
-  uint32_t* cid = base + 2 * a.cap_pad + (qlayout == kQueryChain ? 4 * cs : a.dim_pad);
+  uint32_t* cid = base + 2 * a.cap_pad + (qlayout == kQueryPair ? 2 * pair_stride(a.dim_pad) : a.dim_pad);
   float* cd = reinterpret_cast<float*>(cid + 32 * NPL);
   float* sd = reinterpret_cast<float*>(cid + 64 * NPL);
   uint32_t* sid = cid + 96 * NPL;
@@ -506,7 +520,8 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
         qv[j] = x;
       } else {
         const float y = a.qrot[size_t(qi) * ix.vec_stride + j];
-        qr[qlayout == kQueryChain ? (j & 3) * cs + (j >> 2) : j] = y;
+        // pair-major: half (j mod 4) / 2, position j / 4, chain (j mod 4) odd second
+        qr[qlayout == kQueryPair ? ((j & 3) >> 1) * pair_stride(a.dim_pad) + 2 * (j >> 2) + (j & 1) : j] = y;
       }
     }
     const bool nonfinite = !__all_sync(kFull, finite);
@@ -692,29 +707,53 @@ __global__ void __maxnreg__(search_max_regs(NPL, RCH, EXACT)) search_kernel(cons
       if (!rabitq) {
         l2_rows_warp(ix, qv, cid, m, cd, lane, 0xFFFFFFFFu);
       } else if (RCH == 0) {
-        // wide records: 8 * kWideRecs per round, kWideRecs per lane quad
-        // (candidates i, i + 8, ...), chains reduced with the tile butterfly
-        const uint32_t t = lane & 3;
-        const float* qt = qlayout == kQueryChain ? qr + t * cs : qr;
-        for (uint32_t i0 = 0; i0 < m; i0 += 8 * kWideRecs) {
-          const uint32_t i = i0 + (lane >> 2);
-          float p[kWideRecs], f[kWideRecs][2];
+        if constexpr (BITS == 8) {
+          // wide 8-bit records: 8 * kWideRecs per round, kWideRecs per lane quad
+          // (candidates i, i + 8, ...), chains reduced with the tile butterfly
+          const uint32_t t = lane & 3;
+          for (uint32_t i0 = 0; i0 < m; i0 += 8 * kWideRecs) {
+            const uint32_t i = i0 + (lane >> 2);
+            float p[kWideRecs], f[kWideRecs][2];
 #pragma unroll
-          for (int k = 0; k < kWideRecs; ++k) {
-            p[k] = 0.f;
-            f[k][0] = f[k][1] = 0.f;
+            for (int k = 0; k < kWideRecs; ++k) {
+              p[k] = 0.f;
+              f[k][0] = f[k][1] = 0.f;
+            }
+            if (i < m) {
+              uint32_t c[kWideRecs];
+#pragma unroll
+              for (int k = 0; k < kWideRecs; ++k) c[k] = i + 8u * k < m ? cid[i + 8u * k] : cid[i];
+              estimate_quad_chains8<kWideRecs, kWideBatch>(ix, c, qr, t, p, f);
+            }
+#pragma unroll
+            for (int k = 0; k < kWideRecs; ++k) {
+              const float d = quad_butterfly(p[k]);
+              if (t == 0 && i + 8u * k < m) cd[i + 8u * k] = rabitq_finish(d, f[k][0], f[k][1], q_add, q_k1, 255.0f);
+            }
           }
-          if (i < m) {
-            uint32_t c[kWideRecs];
-#pragma unroll
-            for (int k = 0; k < kWideRecs; ++k) c[k] = i + 8u * k < m ? cid[i + 8u * k] : cid[i];
-            estimate_quad_chains<BITS, kWideRecs, kWideBatch>(ix, c, qt, t, p, f);
-          }
-#pragma unroll
-          for (int k = 0; k < kWideRecs; ++k) {
-            const float d = quad_butterfly(p[k]);
-            if (t == 0 && i + 8u * k < m)
-              cd[i + 8u * k] = rabitq_finish(d, f[k][0], f[k][1], q_add, q_k1, float((1u << BITS) - 1u));
+        } else {
+          // wide 1/2/4-bit records: a lane pair per record, 16 per round; lane h
+          // sums chains 2h and 2h + 1, and the tile sum (s0 + s2) + (s1 + s3)
+          // takes the partner's two chains by shuffle
+          const uint32_t h = lane & 1;
+          const float* qh = qr + h * pair_stride(a.dim_pad);
+          for (uint32_t i0 = 0; i0 < m; i0 += 16) {
+            const uint32_t i = i0 + (lane >> 1);
+            float2 sc = make_float2(0.f, 0.f);
+            float fa = 0.f, fr = 0.f;
+            if (i < m) {
+              const uint32_t g = cid[i];
+              if (h == 0) {
+                const uint32_t* r = reinterpret_cast<const uint32_t*>(rec_row(ix, g));
+                fa = __uint_as_float(__ldg(r + ix.code_words));
+                fr = __uint_as_float(__ldg(r + ix.code_words + 1));
+              }
+              sc = estimate_pair_chains<BITS, kPairBatch>(ix, g, qh, h);
+            }
+            const float o0 = __shfl_xor_sync(kFull, sc.x, 1), o1 = __shfl_xor_sync(kFull, sc.y, 1);
+            if (h == 0 && i < m)
+              cd[i] = rabitq_finish(__fadd_rn(__fadd_rn(sc.x, o0), __fadd_rn(sc.y, o1)), fa, fr, q_add, q_k1,
+                                    float((1u << BITS) - 1u));
           }
         }
         // the guessed next row's records, one hop ahead
@@ -993,7 +1032,7 @@ void launch_rch(int rch, const SearchArgs& a, dim3 g, dim3 b, size_t smem, cudaS
 
 uint32_t search_query_layout(bool exact, uint32_t bits, uint32_t code_words) {
   if (exact) return kQueryRaw;
-  return record_chunks(code_words) == 0 && bits != 8 ? kQueryChain : kQueryRot;
+  return record_chunks(code_words) == 0 && bits != 8 ? kQueryPair : kQueryRot;
 }
 
 bool search_wide_records(bool exact, uint32_t code_words) { return !exact && record_chunks(code_words) == 0; }

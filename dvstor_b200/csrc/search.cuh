@@ -82,19 +82,21 @@ constexpr uint32_t kErrNonFinite = 8u;  // the query held a NaN or an infinity: 
 // How a search warp holds its query in shared memory.
 //   kQueryRaw:   exact_gpu; the query itself, read by every distance.
 //   kQueryRot:   rabitq_gpu; the rotated query q' in dimension order.
-//   kQueryChain: rabitq_gpu with wide 1/2/4-bit records; q' chain-major: chain
-//                t (dims j = t mod 4, the dims one lane of a record's lane quad
-//                sums) is contiguous, so a lane reads its chain 16 bytes at a
-//                time.
+//   kQueryPair:  rabitq_gpu with wide 1/2/4-bit records; q' in two halves,
+//                chains (0, 1) then chains (2, 3) (chain c = dims j = c mod 4),
+//                each half interleaving its two chains by position (dims 4p + 2h
+//                and 4p + 2h + 1 adjacent), so the lane that sums chains 2h and
+//                2h + 1 of a record reads both chains' next two positions with
+//                one 16-byte load.
 // In both rabitq layouts the query itself is not resident during the search:
 // the seed distance reads it from global memory and the rerank copies it into
 // the visited table's words, which are dead by then.
-constexpr uint32_t kQueryRaw = 0, kQueryRot = 1, kQueryChain = 2;
+constexpr uint32_t kQueryRaw = 0, kQueryRot = 1, kQueryPair = 2;
 
-// Words between the starts of two chains of a chain-major q': at least
-// dim_pad / 4, and 4 mod 8 so that the four chains' 16-byte reads at one
-// position fall in four distinct bank groups.
-__host__ __device__ inline uint32_t chain_stride(uint32_t dim_pad) { return ((dim_pad / 4 + 3) & ~7u) + 4; }
+// Words between the starts of the two halves of a pair-major q': at least
+// dim_pad / 2, and 8 mod 16 so that the two halves' 16-byte reads at one
+// position fall in distinct bank groups.
+__host__ __device__ inline uint32_t pair_stride(uint32_t dim_pad) { return 2 * (((dim_pad / 4 + 3) & ~7u) + 4); }
 
 // Words of shared memory one warp of the search kernel uses: the beam (cap_pad
 // distances + ids), the query in the given layout, four candidate staging
@@ -104,7 +106,7 @@ __host__ __device__ inline uint32_t chain_stride(uint32_t dim_pad) { return ((di
 // each starts 16-byte aligned.
 __host__ __device__ inline uint32_t search_warp_words(uint32_t cap_pad, uint32_t dim_pad, uint32_t hcap, uint32_t R,
                                                       uint32_t qlayout) {
-  const uint32_t qwords = qlayout == kQueryChain ? 4 * chain_stride(dim_pad) : dim_pad;
+  const uint32_t qwords = qlayout == kQueryPair ? 2 * pair_stride(dim_pad) : dim_pad;
   const uint32_t twords = qlayout == kQueryRaw ? hcap : (hcap > dim_pad ? hcap : dim_pad);
   return 2 * cap_pad + qwords + (R > 32 ? 256 : 128) + twords;
 }
@@ -149,7 +151,7 @@ cudaError_t launch_search(const SearchArgs& a, uint32_t warps_per_block, uint32_
 cudaError_t search_occupancy(uint32_t bits, uint32_t R, uint32_t code_words, bool exact, uint32_t warps_per_block,
                              size_t smem_bytes, int* blocks_per_sm);
 
-// The query layout (kQueryRaw / kQueryRot / kQueryChain) of the search kernel
+// The query layout (kQueryRaw / kQueryRot / kQueryPair) of the search kernel
 // instantiation that serves this mode and record shape.
 uint32_t search_query_layout(bool exact, uint32_t bits, uint32_t code_words);
 

@@ -34,6 +34,9 @@ def cases(oracle, tmp_path_factory):
         "bits8d160": Case(oracle, tmp, "bits8d160", normalized_gaussian(1200, 160, 15), 24, 32, bits=8),
         "bits2d520": Case(oracle, tmp, "bits2d520", normalized_gaussian(800, 520, 16), 16, 32, bits=2),
         "bits1d1040": Case(oracle, tmp, "bits1d1040", normalized_gaussian(600, 1040, 17), 16, 32, bits=1),
+        # wide records whose dimension is not a multiple of 4: partial last words
+        "d301": Case(oracle, tmp, "d301", normalized_gaussian(900, 301, 18), 24, 32),
+        "bits2d490": Case(oracle, tmp, "bits2d490", normalized_gaussian(700, 490, 19), 16, 32, bits=2),
         "ragged": Case(oracle, tmp, "ragged", normalized_gaussian(1500, 30, 7), 16, 32),
         "ip": Case(oracle, tmp, "ip", normalized_gaussian(2000, 48, 8), 16, 32, metric="ip"),
         "shards": Case(oracle, tmp, "shards", uniform_int_data(3000, 32, 9), 24, 48, M=3),
@@ -57,7 +60,8 @@ def run_both(gpu, oracle, case, Q, k, L, mode="rabitq_gpu"):
 @pytest.mark.parametrize("name,L", [("int128", 64), ("gauss96", 64), ("gauss96", 128), ("r48", 100), ("bits2", 32),
                                     ("bits1", 48), ("bits8", 48), ("bits8d30", 32), ("ragged", 40), ("ip", 32),
                                     ("shards", 64), ("d160", 40), ("d256r48", 48), ("d960r48", 200),
-                                    ("bits8d160", 40), ("bits2d520", 32), ("bits1d1040", 32)])
+                                    ("bits8d160", 40), ("bits2d520", 32), ("bits1d1040", 32), ("d301", 40),
+                                    ("bits2d490", 32)])
 @pytest.mark.parametrize("mode", ["rabitq_gpu", "exact_gpu"])
 def test_search_matches_oracle(gpu, oracle, cases, name, L, mode):
     case = cases[name]
