@@ -458,7 +458,7 @@ __device__ __forceinline__ uint32_t lower_bound_smem(const float* a, uint32_t n,
 
 // Wide records: 8-bit records per lane quad per round and words of each in
 // flight per batch; 16-byte chunks of a 1/2/4-bit record in flight per batch.
-constexpr int kWideRecs = 3, kWideBatch = 6, kPairBatch = 10;
+constexpr int kWideRecs = 3, kWideBatch = 6, kPairBatch = 15;
 
 // Register cap of a search_kernel instantiation.  R <= 32 with records of up
 // to 64 bytes in registers (and exact_gpu): 96, five warps per SM
