@@ -19,8 +19,11 @@ vectors) is larger than L2, which is not flushed between steps.
 oracle/, the reference's own code cannot be built here) on the host cores.
 
 The query rotation runs on the tcgen05 tensor cores (`--rotation tensor`, the
-default; the parity leg then gives the oracle the GPU's rotated queries) or on
-the FP32 pipe in the oracle's own order (`--rotation exact`).
+default of the search modes; the parity leg then gives the oracle the GPU's
+rotated queries) or on the FP32 pipe in the oracle's own order (`--rotation
+exact`, the default of `--mode mixed`: its query batches hold a few queries and
+run beside insert kernels, where the tensor-core kernel's large shared-memory
+stage waits for a free SM).
 
 Other rows of the path: `--search-mode exact_gpu` (exact L2 for every
 candidate), `--bits 1|2|8` (the index built with that code width),
@@ -76,9 +79,9 @@ def parse_args():
     ap.add_argument("--alpha", type=float, default=1.2)
     ap.add_argument("--placement", choices=["replicate", "shard"], default="replicate",
                     help="shard: one process over --gpus devices, the index split by slot (run without torchrun)")
-    ap.add_argument("--rotation", choices=["exact", "tensor"], default="tensor",
-                    help="query rotation: tcgen05 tensor cores (3xTF32, the default), or fp32 in the oracle's fixed "
-                         "order")
+    ap.add_argument("--rotation", choices=["exact", "tensor"], default=None,
+                    help="query rotation: tcgen05 tensor cores (3xTF32; the default except in --mode mixed), or fp32 "
+                         "in the oracle's fixed order (the default of --mode mixed)")
     ap.add_argument("--metric", choices=["l2", "ip"], default=None,
                     help="index metric (default: ip for --mode mixed, else l2)")
     ap.add_argument("--clients", type=int, default=16, help="--mode mixed: client threads per GPU")
@@ -90,7 +93,10 @@ def parse_args():
     ap.add_argument("--parity-queries", type=int, default=500,
                     help="queries of the workload checked against the oracle's Vamana::knn after the timed region")
     ap.add_argument("--build-index-only", action="store_true", help=argparse.SUPPRESS)
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.rotation is None:
+        args.rotation = "exact" if args.mode == "mixed" else "tensor"
+    return args
 
 
 def log(*a):
