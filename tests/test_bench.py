@@ -78,3 +78,13 @@ def test_launch_count_follows_the_prepare_kernels():
     assert bench.launches_per_search(_args("--rotation", "exact"), 96) == 2
     assert bench.launches_per_search(_args("--rotation", "exact"), 960) == 3
     assert bench.launches_per_search(_args("--search-mode", "exact_gpu"), 96) == 1
+
+
+def test_rotation_default_per_mode():
+    # the search modes rotate on the tensor cores; the serving mix, whose small
+    # query batches run beside insert kernels, on the FP32 pipe
+    assert _args().rotation == "tensor"
+    assert _args("--mode", "insert").rotation == "tensor"
+    assert _args("--mode", "mixed").rotation == "exact"
+    assert _args("--mode", "mixed", "--rotation", "tensor").rotation == "tensor"
+    assert _args("--rotation", "exact").rotation == "exact"
